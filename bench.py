@@ -1,0 +1,403 @@
+#!/usr/bin/env python3
+"""W4A16 decode benchmark on B200 (one JSON line on rank 0).
+
+Workload (config "decode", the headline): Llama-3-8B decode at M = 1.  One
+step = one token through the 7 projections of all 32 layers
+(q 4096x4096, k/v 4096x1024, o 4096x4096, gate/up 4096x14336, down 14336x4096),
+signed INT4 weights (full-range random words), group-128 fp16 scales
+|N(0,0.02)|+1e-3, fp16 activations N(0,1).  The layers' weights rotate through
+a pool of distinct buffers at least 4x the L2 size, so every launch streams
+its weights from HBM (inputs larger than L2; no flush needed).
+
+value = algorithmic bytes / second over all ranks, algorithmic bytes per
+projection = K*N/2 + (K/128)*N*2 + M*K*2 + M*N*2.
+
+With --gpus N > 1 (torchrun, one process per GPU) every projection is
+column-sharded N ways and the outputs are gathered with NCCL all-gather
+(t4_cuda_b200.shard): the same token, so "scaling" is "strong".
+
+--impl reference times the reference's CPU dequant + matmul path
+(tests/test_fused_gemm_correctness.py:22-36, restated in oracle/cpu_path.py)
+on the host cores, one projection per step.
+"""
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "W4A16 GEMV HBM GB/s (% of 8 TB/s) at M=1; GEMM TFLOPS at M=4096"
+GROUP = 128
+N_LAYERS = 32
+PROJ = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
+        ("gate", 4096, 14336), ("up", 4096, 14336), ("down", 14336, 4096)]
+# projections that read the same activation share one all-gather
+GATHERS = [("x", ["q", "k", "v"]), ("attn", ["o"]), ("x", ["gate", "up"]), ("h", ["down"])]
+ACT_K = {"x": 4096, "attn": 4096, "h": 14336}
+
+
+def alg_bytes(M, K, N, group=GROUP):
+    return K * N // 2 + (K // group) * N * 2 + M * K * 2 + M * N * 2
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary
+    (profiles/gemv_w4_decode.md, line 'traffic_bytes_per_launch <shape> <bytes>')."""
+    p = os.path.join(ROOT, "profiles", "gemv_w4_decode.md")
+    out = {}
+    if os.path.exists(p):
+        for line in open(p):
+            parts = line.strip().strip("`").split()
+            if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch":
+                out[parts[1]] = float(parts[2])
+    return out
+
+
+class ClockSampler:
+    """Polls NVML (SM clock, throttle reasons) on a thread while the timed
+    region runs; the region is too short for nvidia-smi's 200 ms cadence."""
+
+    BITS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, device_index):
+        self.samples, self.reasons, self.max_mhz, self.ok = [], 0, None, False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = torch.cuda.get_device_properties(device_index).uuid
+            self.h = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                hh = pynvml.nvmlDeviceGetHandleByIndex(i)
+                if str(uuid).replace("GPU-", "") in str(pynvml.nvmlDeviceGetUUID(hh)):
+                    self.h = hh
+            if self.h is None:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= self._reasons_fn(self.h)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return None
+        s = sorted(self.samples)
+        return {"sm_mhz": s[len(s) // 2], "sm_max_mhz": self.max_mhz, "samples": len(s),
+                "reasons": [n for b, n in self.BITS.items() if self.reasons & b and n != "gpu_idle"]}
+
+
+# ----------------------------------------------------------------------------- our arm
+def make_layer(rank, world, M, dev, gen):
+    layer = {}
+    for name, K, N in PROJ:
+        n = N // world
+        W = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, n), dtype=torch.int32, device=dev, generator=gen)
+        S = (torch.randn((K // GROUP, n), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+        layer[name] = (W, S)
+    return layer
+
+
+def run_ours(args):
+    from t4_cuda_b200 import ops
+    from t4_cuda_b200.shard import ShardedGroup, ShardedLinear
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    M = args.m
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    layer_bytes_local = sum(K * (N // world) // 2 + (K // GROUP) * (N // world) * 2 for _, K, N in PROJ)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    pool = max(2, math.ceil(4 * l2 / layer_bytes_local))
+    pool = min(pool, N_LAYERS)
+    layers = [make_layer(rank, world, M, dev, gen) for _ in range(pool)]
+    acts = {a: torch.randn((M, k), device=dev, generator=gen).half() for a, k in ACT_K.items()}
+    pg_layers = [{g: ShardedGroup([ShardedLinear(L[n][0], L[n][1], None, "s4") for n in names])
+                  for g, (a, names) in enumerate(GATHERS)} for L in layers]
+
+    def token(act):
+        outs = []
+        for li in range(N_LAYERS):
+            groups = pg_layers[li % pool]
+            for g, (a, names) in enumerate(GATHERS):
+                outs.extend(groups[g](act[a]))
+        return outs
+
+    step_bytes = N_LAYERS * sum(alg_bytes(M, K, N) for _, K, N in PROJ)
+    launches_per_step = N_LAYERS * len(PROJ)
+
+    use_graph = world == 1
+    if use_graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                token(acts)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            token(acts)
+        run_step = graph.replay
+    else:
+        def run_step():
+            token(acts)
+
+    def barrier_sync():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        run_step()
+    barrier_sync()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            run_step()
+        end.record()
+        end.synchronize()
+    barrier_sync()
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = step_bytes * args.steps / (ms * 1e-3) / 1e9
+
+    # ---- per-shape breakdown (one GPU): a graph of `pool` launches of one shape
+    per_shape = {}
+    if world == 1:
+        for name, K, N in PROJ:
+            a = acts["h"] if name == "down" else acts["x"]
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for L in layers:
+                    ops.fused_w4a16_gemm_s4(a, L[name][0], L[name][1], None)
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 20
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * len(layers))
+            per_shape[f"{name}_{K}x{N}"] = {"us": round(us, 3), "GB/s": round(alg_bytes(M, K, N) / us / 1e3, 1)}
+            del g
+
+    # ---- end to end through the public API, host buffers, copies timed
+    pin = {a: t.cpu().pin_memory() for a, t in acts.items()}
+    dev_in = {a: torch.empty_like(t) for a, t in acts.items()}
+    outs_eager = token(dev_in)
+    out_host = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs_eager]
+    h2d = sum(t.numel() * 2 for t in acts.values())
+    d2h = sum(o.numel() * 2 for o in out_host)
+
+    def e2e_step():
+        for a in acts:
+            dev_in[a].copy_(pin[a], non_blocking=True)
+        outs = token(dev_in)
+        for o, hbuf in zip(outs, out_host):
+            hbuf.copy_(o, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier_sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    e1.synchronize()
+    barrier_sync()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = step_bytes * args.steps / (e2e_ms * 1e-3) / 1e9
+
+    if use_graph:
+        del graph
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = load_peaks()
+    traffic = load_traffic()
+    achieved = step_bytes / (ms_per_step * 1e-3) / 1e9 if world == 1 else None
+    roof = None
+    if world == 1:
+        tr = traffic.get("decode_step")
+        roof = {"bound": "hbm", "kernel": "gemv_w4_kernel", "achieved": round(achieved, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
+                else "fallback 6650 GB/s",
+                "traffic": (tr / launches_per_step) if tr else None,
+                "algorithmic_bytes_per_launch": step_bytes / launches_per_step,
+                "note": "timed region holds only gemv_w4_kernel launches; duration per launch = region / launches"}
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 (int4 weights, fp32 accumulate)",
+        "data": "synthetic",
+        "config": {"workload": "decode: Llama-3-8B token, 32 layers x 7 projections, M=1, s4 g128",
+                   "M": M, "group": GROUP, "layers_per_step": N_LAYERS, "distinct_weight_layers": pool,
+                   "weight_pool_bytes": pool * layer_bytes_local, "l2_bytes": l2,
+                   "l2_policy": "weights rotate through a pool >= 4x L2 (inputs larger than L2)",
+                   "parallelism": f"column-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "frac_of_8TBs": round(value / 8000.0, 4)},
+        "gpu_launches": launches_per_step * args.steps,
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
+                "api": "t4_kernels.fused_w4a16_gemm_s4 (eager, pinned host buffers)"},
+        "per_shape": per_shape,
+        "roofline": roof,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- CPU path
+def cpu_projection(name, K, N, M, gen):
+    A = torch.randn((M, K), generator=gen).half()
+    W = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, generator=gen)
+    S = (torch.randn((K // GROUP, N), generator=gen).abs() * 0.02 + 1e-3).half()
+    return A, W, S
+
+
+def cpu_baseline(budget_s=20.0, M=1):
+    """The reference's CPU dequant + matmul (oracle/cpu_path.py) over the 7
+    projections of one layer, as many as fit in the time budget."""
+    from oracle import cpu_path
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(7)
+    nbytes, secs, done = 0, 0.0, []
+    cpu_path.w4_gemm(*cpu_projection("warm", 512, 512, M, gen), None, True)
+    for name, K, N in PROJ:
+        A, W, S = cpu_projection(name, K, N, M, gen)
+        t0 = time.perf_counter()
+        cpu_path.w4_gemm(A, W, S, None, True)
+        secs += time.perf_counter() - t0
+        nbytes += alg_bytes(M, K, N)
+        done.append(name)
+        if secs > budget_s:
+            break
+    return {"value": round(nbytes / secs / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "seconds": round(secs, 2),
+            "sample": f"Llama-3-8B layer projections {'/'.join(done)} at M={M} (one layer = 1/32 of a step), "
+                      "torch CPU dequant (q*s -> fp16) + fp32 matmul as tests/test_fused_gemm_correctness.py:22-36"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cpu_path
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(7)
+    M = args.m
+    inputs = [cpu_projection(n, K, N, M, gen) for n, K, N in PROJ]
+    for i in range(args.warmup):
+        A, W, S = inputs[i % len(PROJ)]
+        cpu_path.w4_gemm(A, W, S, None, True)
+    nbytes, secs = 0, 0.0
+    for i in range(args.steps):
+        (name, K, N), (A, W, S) = PROJ[i % len(PROJ)], inputs[i % len(PROJ)]
+        t0 = time.perf_counter()
+        cpu_path.w4_gemm(A, W, S, None, True)
+        secs += time.perf_counter() - t0
+        nbytes += alg_bytes(M, K, N)
+    value = nbytes / secs / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (fp16 weights)",
+            "data": "synthetic",
+            "config": {"workload": "decode: Llama-3-8B projections, M=1, s4 g128 (one projection per step)",
+                       "M": M, "group": GROUP},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+                             "kind": "port",
+                             "sample": "one Llama-3-8B projection per step, rotating q,k,v,o,gate,up,down"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--m", type=int, default=1, help="activation rows (decode batch)")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)     # at least 3 untimed warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,112 @@
+/*
+ * t4b200.h -- C ABI of the B200 (sm_100a) W4A16 / INT3 quantized-matmul library.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, a cudaStream_t; NULL = the legacy default stream),
+ * enqueues its kernels asynchronously and returns a status code (T4B_OK = 0).
+ * Nothing throws across this boundary and nothing here allocates device memory.
+ * Element types: "f16" = IEEE binary16 (uint16 storage), "words" = uint32
+ * (int32 in torch) holding packed weights.
+ *
+ * Each function replaces one launcher of the reference project
+ * (kridaydave/t4-cuda); the citation names the reference declaration it stands
+ * in for and the pybind op that called it (src/bindings.cpp:252-260).
+ */
+#ifndef T4B200_H
+#define T4B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+    T4B_OK = 0,
+    T4B_ERR_INVALID_VALUE = 1,   /* a size, group or mode argument is out of range      */
+    T4B_ERR_NULL_POINTER = 2,    /* a required pointer is NULL                          */
+    T4B_ERR_MISALIGNED = 3,      /* a pointer breaks the alignment the op documents     */
+    T4B_ERR_UNSUPPORTED = 4,     /* shape/option combination this build does not serve */
+    T4B_ERR_CUDA = 5             /* a CUDA runtime call or kernel launch failed         */
+};
+
+/* Dequantization arithmetic (argument `mode` of the t4b_dequantize_* calls). */
+enum {
+    T4B_MODE_CONTRACT = 0,  /* fp16_rn(fp32_rn((q - z) * s)): what the reference tests assert */
+    T4B_MODE_MAGIC = 1      /* bit-exact with the reference GPU kernels' LOP3 + fma.rn.f16x2    */
+};
+
+/* Human-readable text for a status code (static storage). */
+const char* t4b_status_string(int status);
+
+/* The cudaError_t of the most recent T4B_ERR_CUDA on the calling thread (0 if none). */
+int t4b_last_cuda_error(void);
+
+/* Library ABI version: (major << 16) | minor. */
+int t4b_version(void);
+
+/* ---- flat dequantization ----------------------------------------------
+ * out[8*i + j] = dequant(nibble j of words[i], scales[i], zero_points[i]).
+ * Scale / zero point are per WORD (lop3_dequant.cu:19-21); num_scales and
+ * num_zero_points are either num_words or 1 (broadcast); num_zero_points = 0
+ * (zero_points may then be NULL) means zero.  out holds num_words*8 f16
+ * (u4, s4), num_words*10 (s3) or num_words*4 (fp8).  num_words may be 0.
+ */
+
+/* replaces launch_lop3_dequant_u4 (src/kernels/lop3_dequant.h:126-127), op dequantize_u4 */
+int t4b_dequantize_u4(const void* words, const void* scales, const void* zero_points,
+                      void* out, int64_t num_words, int64_t num_scales,
+                      int64_t num_zero_points, int mode, void* stream);
+
+/* replaces launch_lop3_dequant_s4 (src/kernels/lop3_dequant.h:129-130), op dequantize_s4 */
+int t4b_dequantize_s4(const void* words, const void* scales, const void* zero_points,
+                      void* out, int64_t num_words, int64_t num_scales,
+                      int64_t num_zero_points, int mode, void* stream);
+
+/* replaces launch_lop3_dequant_s3 (src/kernels/lop3_dequant.h:132-133), op dequantize_s3 */
+int t4b_dequantize_s3(const void* words, const void* scales, const void* zero_points,
+                      void* out, int64_t num_words, int64_t num_scales,
+                      int64_t num_zero_points, int mode, void* stream);
+
+/* replaces launch_lop3_dequant_fp8 (src/kernels/lop3_dequant.h:135-136), op dequantize_fp8 */
+int t4b_dequantize_fp8(const void* words, const void* scales, void* out,
+                       int64_t num_words, int64_t num_scales, int mode, void* stream);
+
+/* ---- fused W4A16 matmul -----------------------------------------------
+ * C[M, N] (f16, row-major) = A[M, K] (f16, row-major) x dequant(W)[K, N]
+ * with W_packed int32 [K/8, N] row-major, K row 8*kw + j in nibble j of word
+ * (kw, n).  scales / zero_points are f16 [K/group_size, N] row-major; the
+ * reference's per-column (1, N) tensors are group_size = K.  zero_points may
+ * be NULL (zero).  Requirements: M, N >= 1; K >= 8, K % 8 == 0;
+ * group_size % 8 == 0 and K % group_size == 0.  Weights are rounded to f16
+ * by the contract rule; products and sums are fp32.
+ */
+
+/* replaces launch_fused_w4a16_gemm_u4 (src/kernels/fused_w4a16_gemm.h:24-31), op fused_w4a16_gemm_u4 */
+int t4b_fused_w4a16_gemm_u4(const void* A, const void* W_packed, const void* scales,
+                            const void* zero_points, void* C, int M, int N, int K,
+                            int group_size, void* stream);
+
+/* replaces launch_fused_w4a16_gemm_s4 (src/kernels/fused_w4a16_gemm.h:39-46), op fused_w4a16_gemm_s4 */
+int t4b_fused_w4a16_gemm_s4(const void* A, const void* W_packed, const void* scales,
+                            const void* zero_points, void* C, int M, int N, int K,
+                            int group_size, void* stream);
+
+/* ---- H17 fused INT3 GEMV ------------------------------------------------
+ * C[M, N] (f16) = A[M, K] (f16) x dequant_s3(W)[K, N], W_packed int32 [K/10, N],
+ * element i of word (kw, n) = K row 10*kw + i at bits 3i..3i+2.
+ * scales / zero_points f16 [ceil(K/group_size), N]; zero_points may be NULL.
+ * Requirements: M, N >= 1; K >= 10, K % 10 == 0; group_size >= 1.
+ */
+
+/* replaces launch_h17_gemv_s3 (src/kernels/h17_mega_kernel.h:22-30), op fused_h17_gemv_s3 */
+int t4b_fused_h17_gemv_s3(const void* A, const void* W_packed, const void* scales,
+                          const void* zero_points, void* C, int M, int N, int K,
+                          int group_size, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* T4B200_H */

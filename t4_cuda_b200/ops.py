@@ -1,0 +1,251 @@
+"""The seven ops of the reference's ``t4_kernels`` extension, on B200.
+
+Same names, argument order, output shapes and error type (RuntimeError, as
+TORCH_CHECK raises) as src/bindings.cpp:8-260 of kridaydave/t4-cuda.  Every op
+validates its tensors, allocates its output with ``torch.empty`` on the input's
+device and enqueues the CUDA kernel of libt4b200.so on the current stream of
+that device, asynchronously.  There is no CPU path: CPU tensors are rejected
+exactly as the reference rejects them.
+
+Extensions, all backward compatible (trailing keyword arguments):
+  * ``dequantize_*(..., mode="contract")``: "contract" = fp16(fp32((q-z)*s)),
+    what the reference tests assert; "magic" = the reference GPU kernels'
+    fp16-FMA arithmetic, bit for bit.  Scale / zero point may also have 1
+    element (broadcast), as the reference's CPU oracle allows.
+  * ``fused_w4a16_gemm_*``: scales / zero points of shape (N,), (1, N) or
+    grouped (K/g, N); zero_points may be None or empty (zero).
+  * ``fused_h17_gemv_s3(..., group_size=100)``: any group size (the reference
+    hard-codes 100).
+"""
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "dequantize_u4", "dequantize_s4", "dequantize_s3", "dequantize_fp8",
+    "fused_w4a16_gemm_u4", "fused_w4a16_gemm_s4", "fused_h17_gemv_s3",
+]
+
+
+def _check(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream_ptr(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _on_device:
+    """Make ``device`` current for the launch (like at::cuda::CUDAGuard)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device):
+        self.idx = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+def _mode(mode):
+    _check(mode in _lib.MODES, f"mode must be one of {sorted(_lib.MODES)}, got {mode!r}")
+    return _lib.MODES[mode]
+
+
+def _aligned16(t):
+    """Contiguous tensor whose data pointer is 16-byte aligned (copy if not)."""
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+# --------------------------------------------------------------- dequantize
+def _dequant(name, per_word_out, packed_weights, scales, zero_points, mode):
+    _check(packed_weights.is_cuda, "packed_weights must be a CUDA tensor")
+    _check(scales.is_cuda, "scales must be a CUDA tensor")
+    has_zp = zero_points is not None
+    if has_zp:
+        _check(zero_points.is_cuda, "zero_points must be a CUDA tensor")
+    _check(packed_weights.dtype == torch.int32, "packed_weights must be Int32")
+    _check(scales.dtype == torch.float16, "scales must be FP16")
+    if has_zp:
+        _check(zero_points.dtype == torch.float16, "zero_points must be FP16")
+    dev = packed_weights.device
+    _check(scales.device == dev and (not has_zp or zero_points.device == dev),
+           "all tensors must be on the same device")
+    n = packed_weights.numel()
+    _check(scales.numel() in (1, n), f"scales must have 1 or {n} elements (one per packed word), got {scales.numel()}")
+    nz = zero_points.numel() if has_zp else 0
+    _check(nz in (0, 1, n), f"zero_points must have 1 or {n} elements (one per packed word), got {nz}")
+    out = torch.empty(n * per_word_out, dtype=torch.float16, device=dev)
+    if n == 0:
+        return out
+    w = packed_weights.contiguous()
+    s = scales.contiguous()
+    z = zero_points.contiguous() if nz else None
+    m = _mode(mode)
+    lib = _lib.load()
+    with _on_device(dev):
+        st = getattr(lib, name)(w.data_ptr(), s.data_ptr(), z.data_ptr() if z is not None else None,
+                                out.data_ptr(), n, s.numel(), nz, m, _stream_ptr(dev))
+    _lib.check(st, name)
+    return out
+
+
+def dequantize_u4(packed_weights, scales, zero_points, mode="contract"):
+    """Unsigned INT4 dequantization; out[8i + j] = (nibble j of word i - z_i) * s_i.
+    Mirrors bindings.cpp:8-33 (dequantize_lop3_u4_cuda)."""
+    return _dequant("t4b_dequantize_u4", 8, packed_weights, scales, zero_points, mode)
+
+
+def dequantize_s4(packed_weights, scales, zero_points, mode="contract"):
+    """Signed (two's complement) INT4 dequantization.  Mirrors bindings.cpp:35-60."""
+    return _dequant("t4b_dequantize_s4", 8, packed_weights, scales, zero_points, mode)
+
+
+def dequantize_s3(packed_weights, scales, zero_points, mode="contract"):
+    """Signed INT3 dequantization, 10 values per word (bits 3i..3i+2).
+    Mirrors bindings.cpp:134-159."""
+    return _dequant("t4b_dequantize_s3", 10, packed_weights, scales, zero_points, mode)
+
+
+def dequantize_fp8(packed_weights, scales, mode="contract"):
+    """FP8-E4M3 (4 bytes per word) dequantization.  Mirrors bindings.cpp:161-183."""
+    _check(packed_weights.is_cuda, "packed_weights must be a CUDA tensor")
+    _check(scales.is_cuda, "scales must be a CUDA tensor")
+    _check(packed_weights.dtype == torch.int32, "packed_weights must be Int32")
+    _check(scales.dtype == torch.float16, "scales must be FP16")
+    dev = packed_weights.device
+    _check(scales.device == dev, "all tensors must be on the same device")
+    n = packed_weights.numel()
+    _check(scales.numel() in (1, n), f"scales must have 1 or {n} elements (one per packed word), got {scales.numel()}")
+    out = torch.empty(n * 4, dtype=torch.float16, device=dev)
+    if n == 0:
+        return out
+    w = packed_weights.contiguous()
+    s = scales.contiguous()
+    m = _mode(mode)
+    with _on_device(dev):
+        st = _lib.load().t4b_dequantize_fp8(w.data_ptr(), s.data_ptr(), out.data_ptr(), n, s.numel(), m,
+                                            _stream_ptr(dev))
+    _lib.check(st, "t4b_dequantize_fp8")
+    return out
+
+
+# --------------------------------------------------------------- fused GEMM
+def _group_rows(t, N, K, what):
+    """(N,) / (1, N) / (G, N) -> number of rows G, with checks."""
+    _check(t.dim() in (1, 2), f"{what} must be 1-D (N,) or 2-D (K/group, N)")
+    if t.dim() == 1:
+        _check(t.numel() == N, f"{what} of shape (N,) must have N={N} elements, got {t.numel()}")
+        return 1
+    _check(t.size(1) == N, f"{what} must have N={N} columns, got {t.size(1)}")
+    G = t.size(0)
+    _check(G >= 1 and K % G == 0, f"{what}: {G} groups must divide K={K}")
+    gs = K // G
+    _check(gs % 8 == 0, f"{what}: group size K/{G}={gs} must be a multiple of 8")
+    return G
+
+
+def _fused(name, A, W_packed, scales, zero_points):
+    _check(A.is_cuda, "A must be a CUDA tensor")
+    _check(W_packed.is_cuda, "W_packed must be a CUDA tensor")
+    _check(scales.is_cuda, "scales must be a CUDA tensor")
+    has_zp = zero_points is not None and zero_points.numel() > 0
+    if has_zp:
+        _check(zero_points.is_cuda, "zero_points must be a CUDA tensor")
+        _check(zero_points.dtype == torch.float16, "zero_points must be FP16")
+    _check(A.dtype == torch.float16, "A must be FP16")
+    _check(W_packed.dtype == torch.int32, "W_packed must be Int32")
+    _check(scales.dtype == torch.float16, "scales must be FP16")
+    _check(A.dim() == 2, "A must be a 2-D (M, K) tensor")
+    _check(W_packed.dim() == 2, "W_packed must be a 2-D (K/8, N) tensor")
+    dev = A.device
+    _check(W_packed.device == dev and scales.device == dev and (not has_zp or zero_points.device == dev),
+           "all tensors must be on the same device")
+    M, K = A.shape
+    N = W_packed.size(1)
+    _check(M > 0 and N > 0 and K > 0, "Dimensions M, N, K must be positive")
+    _check(K % 8 == 0, "K must be a multiple of 8 (8 INT4 values per int32 word)")
+    _check(W_packed.size(0) == K // 8, f"W_packed must have K/8={K // 8} rows, got {W_packed.size(0)}")
+    G = _group_rows(scales, N, K, "scales")
+    if has_zp:
+        _check(_group_rows(zero_points, N, K, "zero_points") == G, "zero_points must have the same shape as scales")
+    A_ = _aligned16(A)
+    W_ = W_packed.contiguous()
+    S_ = scales.contiguous()
+    Z_ = zero_points.contiguous() if has_zp else None
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    with _on_device(dev):
+        st = getattr(_lib.load(), name)(A_.data_ptr(), W_.data_ptr(), S_.data_ptr(),
+                                        Z_.data_ptr() if Z_ is not None else None, C.data_ptr(),
+                                        M, N, K, K // G, _stream_ptr(dev))
+    _lib.check(st, name)
+    return C
+
+
+def fused_w4a16_gemm_u4(A, W_packed, scales, zero_points):
+    """C = A @ dequant_u4(W_packed).  Mirrors bindings.cpp:64-97."""
+    return _fused("t4b_fused_w4a16_gemm_u4", A, W_packed, scales, zero_points)
+
+
+def fused_w4a16_gemm_s4(A, W_packed, scales, zero_points):
+    """C = A @ dequant_s4(W_packed).  Mirrors bindings.cpp:99-132."""
+    return _fused("t4b_fused_w4a16_gemm_s4", A, W_packed, scales, zero_points)
+
+
+# --------------------------------------------------------------- H17 INT3 GEMV
+def fused_h17_gemv_s3(A, W_packed, scales, zero_points, group_size=100):
+    """C = A @ dequant_s3(W_packed) with per-group scales / zero points.
+    Mirrors bindings.cpp:185-250 check for check; ``group_size`` generalises
+    the reference's fixed group of 100 (h17_mega_kernel.cu:22)."""
+    _check(A.is_cuda, "A must be a CUDA tensor")
+    _check(W_packed.is_cuda, "W_packed must be a CUDA tensor")
+    _check(scales.is_cuda, "scales must be a CUDA tensor")
+    has_zp = zero_points is not None and zero_points.numel() > 0
+    if has_zp:
+        _check(zero_points.is_cuda, "zero_points must be a CUDA tensor")
+        _check(zero_points.dtype == torch.float16, "zero_points must be FP16")
+        _check(zero_points.is_contiguous(), "zero_points must be contiguous")
+    _check(A.is_contiguous(), "A must be contiguous")
+    _check(W_packed.is_contiguous(), "W_packed must be contiguous")
+    _check(scales.is_contiguous(), "scales must be contiguous")
+    _check(A.dtype == torch.float16, "A must be FP16")
+    _check(W_packed.dtype == torch.int32, "W_packed must be Int32")
+    _check(scales.dtype == torch.float16, "scales must be FP16")
+    _check(A.dim() in (1, 2), "A must be 1D or 2D tensor")
+    _check(W_packed.dim() == 2, "W_packed must be a 2D tensor")
+    dev = A.device
+    _check(W_packed.device == dev and scales.device == dev and (not has_zp or zero_points.device == dev),
+           "all tensors must be on the same device")
+    M = 1 if A.dim() == 1 else A.size(0)
+    K = A.size(0) if A.dim() == 1 else A.size(1)
+    N = W_packed.size(1)
+    _check(M > 0 and N > 0 and K > 0, "Dimensions M, N, K must be positive")
+    _check(K % 10 == 0, "K must be a multiple of 10 for H17 int3 packing")
+    _check(W_packed.size(0) == K // 10, "W_packed first dim must equal K/10 (canonical H17 layout)")
+    _check(isinstance(group_size, int) and group_size >= 1, "group_size must be a positive int")
+    num_groups = (K + group_size - 1) // group_size
+    _check(scales.numel() == num_groups * N,
+           f"scales must have num_groups * N elements (num_groups = ceil(K/{group_size}))")
+    if has_zp:
+        _check(zero_points.numel() == num_groups * N, "zero_points must have num_groups * N elements")
+    A_ = _aligned16(A)
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    with _on_device(dev):
+        st = _lib.load().t4b_fused_h17_gemv_s3(A_.data_ptr(), W_packed.data_ptr(), scales.data_ptr(),
+                                               zero_points.data_ptr() if has_zp else None, C.data_ptr(),
+                                               M, N, K, group_size, _stream_ptr(dev))
+    _lib.check(st, "t4b_fused_h17_gemv_s3")
+    return C

@@ -1,0 +1,103 @@
+"""Column-sharded (N-split) W4A16 / INT3 projections over torch.distributed.
+
+The reference has no multi-GPU code; this is the one multi-GPU piece the
+library adds.  Rank r of a G-rank group holds columns [r*N/G, (r+1)*N/G) of
+every packed weight (word columns are sliced; the packed layout is unchanged)
+and the matching scale / zero-point columns.  A forward pass runs the
+single-GPU kernel on the local columns and gathers the G output slices with
+one ``all_gather_into_tensor`` over NCCL (NVLink / NVSwitch on a B200 node).
+Several projections that consume the same activation (q/k/v, gate/up) can
+share one gather (``ShardedGroup``), which matters at M = 1 where the gather's
+latency, not its bytes, dominates.
+
+Collectives are issued in the same order on every rank; no rank skips one.
+"""
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+
+def shard_bounds(N, rank, world):
+    """Column range of ``rank``; N must divide evenly (every Llama projection does)."""
+    if N % world:
+        raise ValueError(f"N={N} is not divisible by the world size {world}")
+    n = N // world
+    return rank * n, (rank + 1) * n
+
+
+def shard_columns(t, rank, world):
+    """Columns of a 2-D tensor (packed words, scales or zero points) owned by ``rank``."""
+    if t is None:
+        return None
+    if t.dim() == 1:
+        t = t.reshape(1, -1)
+    lo, hi = shard_bounds(t.size(1), rank, world)
+    return t[:, lo:hi].contiguous()
+
+
+class ShardedLinear:
+    """One column-sharded projection y = x @ dequant(W)."""
+
+    def __init__(self, W_local, scales_local, zero_points_local=None, fmt="s4", group_size=100,
+                 process_group=None):
+        if fmt not in ("s4", "u4", "s3"):
+            raise ValueError("fmt must be 's4', 'u4' or 's3'")
+        self.W, self.S, self.Z = W_local, scales_local, zero_points_local
+        self.fmt, self.group_size = fmt, group_size
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.n_local = W_local.size(1)
+
+    @classmethod
+    def from_full(cls, W, scales, zero_points=None, fmt="s4", group_size=100, process_group=None):
+        world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        return cls(shard_columns(W, rank, world), shard_columns(scales, rank, world),
+                   shard_columns(zero_points, rank, world), fmt, group_size, process_group)
+
+    def local(self, x):
+        """This rank's [M, N/G] slice of the output."""
+        if self.fmt == "s4":
+            return ops.fused_w4a16_gemm_s4(x, self.W, self.S, self.Z)
+        if self.fmt == "u4":
+            return ops.fused_w4a16_gemm_u4(x, self.W, self.S, self.Z)
+        z = self.Z if self.Z is not None else torch.empty(0, dtype=torch.float16, device=x.device)
+        return ops.fused_h17_gemv_s3(x, self.W, self.S, z, group_size=self.group_size)
+
+    def __call__(self, x):
+        return ShardedGroup([self], self.pg)(x)[0]
+
+
+class ShardedGroup:
+    """Projections that read the same activation; their local outputs are
+    packed into one buffer and gathered with a single collective."""
+
+    def __init__(self, linears, process_group=None):
+        self.linears = list(linears)
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+
+    def __call__(self, x):
+        locals_ = [lin.local(x) for lin in self.linears]
+        if self.world == 1:
+            return locals_
+        M = locals_[0].size(0)
+        widths = [t.size(1) for t in locals_]
+        packed = torch.cat(locals_, dim=1) if len(locals_) > 1 else locals_[0]
+        gathered = torch.empty((self.world, M, packed.size(1)), dtype=packed.dtype, device=packed.device)
+        dist.all_gather_into_tensor(gathered, packed.contiguous(), group=self.pg)
+        return unpack_gathered(gathered, widths)
+
+
+def unpack_gathered(gathered, widths):
+    """[G, M, sum(widths)] rank-major slices -> one [M, G*w] tensor per projection,
+    columns in rank order (rank r's slice is columns [r*w, (r+1)*w))."""
+    G, M, _ = gathered.shape
+    outs, off = [], 0
+    for w in widths:
+        part = gathered[:, :, off:off + w]                    # [G, M, w]
+        outs.append(part.permute(1, 0, 2).reshape(M, G * w))  # a copy only when M > 1 or several parts
+        off += w
+    return outs

@@ -4,7 +4,10 @@
  * Every entry point takes plain device pointers, sizes and a CUDA stream
  * (passed as void*, a cudaStream_t; NULL = the legacy default stream),
  * enqueues its kernels asynchronously and returns a status code (T4B_OK = 0).
- * Nothing throws across this boundary and nothing here allocates device memory.
+ * Nothing throws across this boundary.  The caller owns every input and output
+ * buffer; the W4A16 matmul additionally uses a small scratch workspace that the
+ * library allocates itself, once per (device, stream), on the first call that
+ * needs it (make that first call outside CUDA-graph capture).
  * Element types: "f16" = IEEE binary16 (uint16 storage), "words" = uint32
  * (int32 in torch) holding packed weights.
  *
@@ -45,6 +48,22 @@ int t4b_last_cuda_error(void);
 
 /* Library ABI version: (major << 16) | minor. */
 int t4b_version(void);
+
+/* Reads (and, if `clear`, resets) the device error word of the workspace this
+ * library keeps for `stream` on the current device: bit 0 = a kernel gave up a
+ * bounded wait (its output is then invalid).  Synchronizes `stream`; do not
+ * call while the stream is being captured.  No library extension: this has no
+ * counterpart in the reference, which has no device-side error reporting. */
+int t4b_device_error(void* stream, unsigned* out, int clear);
+
+/* Kernel selection for the W4A16 matmul (argument of t4b_set_gemv_kernel). */
+enum {
+    T4B_GEMV_AUTO = 0,     /* TMA-streamed SM-balanced kernel where it applies, else generic */
+    T4B_GEMV_GENERIC = 1   /* always the generic register-streaming kernel (for comparison)  */
+};
+/* Sets the process-wide choice; returns the previous one (-1: bad argument).
+ * No counterpart in the reference (it has a single kernel). */
+int t4b_set_gemv_kernel(int which);
 
 /* ---- flat dequantization ----------------------------------------------
  * out[8*i + j] = dequant(nibble j of words[i], scales[i], zero_points[i]).
@@ -97,7 +116,8 @@ int t4b_fused_w4a16_gemm_s4(const void* A, const void* W_packed, const void* sca
  * C[M, N] (f16) = A[M, K] (f16) x dequant_s3(W)[K, N], W_packed int32 [K/10, N],
  * element i of word (kw, n) = K row 10*kw + i at bits 3i..3i+2.
  * scales / zero_points f16 [ceil(K/group_size), N]; zero_points may be NULL.
- * Requirements: M, N >= 1; K >= 10, K % 10 == 0; group_size >= 1.
+ * Requirements: M, N >= 1; K >= 10, K % 10 == 0; group_size >= 10 (so that a
+ * word spans at most two groups; smaller groups return T4B_ERR_UNSUPPORTED).
  */
 
 /* replaces launch_h17_gemv_s3 (src/kernels/h17_mega_kernel.h:22-30), op fused_h17_gemv_s3 */

@@ -17,6 +17,8 @@ from .ops import (  # noqa: F401
     fused_w4a16_gemm_u4,
     fused_w4a16_gemm_s4,
     fused_h17_gemv_s3,
+    set_gemv_kernel,
+    device_error,
 )
 from ._lib import LIB_PATH, T4BError, load as load_library  # noqa: F401
 

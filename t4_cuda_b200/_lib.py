@@ -56,6 +56,10 @@ def load():
         lib.t4b_last_cuda_error.restype = ctypes.c_int
         lib.t4b_version.argtypes = []
         lib.t4b_version.restype = ctypes.c_int
+        lib.t4b_set_gemv_kernel.argtypes = [ctypes.c_int]
+        lib.t4b_set_gemv_kernel.restype = ctypes.c_int
+        lib.t4b_device_error.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
+        lib.t4b_device_error.restype = ctypes.c_int
         _lib = lib
     return _lib
 

@@ -1,8 +1,15 @@
 // Library-wide C ABI plumbing: status strings, the per-thread CUDA error
-// record and the cached per-device SM count used to size grids.
+// record, the cached per-device SM count used to size grids, the per-stream
+// workspace of the streaming GEMV, and TMA tensor-map encoding.
 #include "common.cuh"
+#include "tma.cuh"
+#include "workspace.h"
 
+#include <cudaTypedefs.h>
+
+#include <map>
 #include <mutex>
+#include <utility>
 
 namespace t4b {
 
@@ -10,6 +17,17 @@ namespace {
 thread_local int g_last_cuda_error = 0;
 std::mutex g_sm_mutex;
 int g_sm_counts[64] = {0};
+
+struct WsBuf {
+    void* base = nullptr;
+    size_t counter_words = 0;
+    size_t part_floats = 0;
+};
+std::mutex g_ws_mutex;
+std::map<std::pair<int, cudaStream_t>, WsBuf> g_ws;
+
+constexpr size_t kHeaderBytes = 256;
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 }  // namespace
 
 int record_cuda_error(cudaError_t err) {
@@ -31,6 +49,78 @@ int sm_count() {
     return n;
 }
 
+int acquire_workspace(cudaStream_t stream, size_t counter_words, size_t part_floats, Workspace* ws) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    std::lock_guard<std::mutex> lock(g_ws_mutex);
+    WsBuf& buf = g_ws[{dev, stream}];
+    if (!buf.base || buf.counter_words < counter_words || buf.part_floats < part_floats) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        e = cudaStreamIsCapturing(stream, &cap);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        if (cap != cudaStreamCaptureStatusNone) return T4B_ERR_UNSUPPORTED;
+        // Grow with headroom; the previous buffer may still be in use by queued
+        // kernels, so it is kept (not freed) -- growth is rare and bounded.
+        const size_t cw = round_up(std::max(counter_words * 2, std::max(buf.counter_words, (size_t)65536)), 64);
+        const size_t pf = round_up(std::max(part_floats * 2, std::max(buf.part_floats, (size_t)(1 << 20))), 64);
+        const size_t bytes = kHeaderBytes + cw * 4 + pf * 4;
+        void* p = nullptr;
+        e = cudaMalloc(&p, bytes);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        e = cudaMemsetAsync(p, 0, kHeaderBytes + cw * 4, stream);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        buf.base = p;
+        buf.counter_words = cw;
+        buf.part_floats = pf;
+    }
+    char* base = static_cast<char*>(buf.base);
+    ws->error = reinterpret_cast<unsigned*>(base);
+    ws->counters = reinterpret_cast<unsigned*>(base + kHeaderBytes);
+    ws->part = reinterpret_cast<float*>(base + kHeaderBytes + buf.counter_words * 4);
+    return T4B_OK;
+}
+
+// ------------------------------------------------------------- tensor maps
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t esize, const void* base, uint64_t rows,
+                  uint64_t cols, uint32_t box_rows, uint32_t box_cols) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    if ((cols * esize) % 16 != 0 || (reinterpret_cast<uintptr_t>(base) % 16) != 0) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * esize};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+bool make_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                      uint32_t box_cols) {
+    return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, base, rows, cols, box_rows, box_cols);
+}
+
+bool make_tmap_f16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                      uint32_t box_cols) {
+    return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, rows, cols, box_rows, box_cols);
+}
+
 }  // namespace t4b
 
 extern "C" {
@@ -49,6 +139,26 @@ const char* t4b_status_string(int status) {
 
 int t4b_last_cuda_error(void) { return t4b::g_last_cuda_error; }
 
-int t4b_version(void) { return (1 << 16) | 0; }
+int t4b_version(void) { return (1 << 16) | 1; }
+
+int t4b_device_error(void* stream, unsigned* out, int clear) {
+    if (!out) return T4B_ERR_NULL_POINTER;
+    *out = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return t4b::record_cuda_error(e);
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(t4b::g_ws_mutex);
+        auto it = t4b::g_ws.find({dev, static_cast<cudaStream_t>(stream)});
+        if (it == t4b::g_ws.end()) return T4B_OK;
+        base = it->second.base;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    e = cudaMemcpyAsync(out, base, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(base, 0, sizeof(unsigned), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? T4B_OK : t4b::record_cuda_error(e);
+}
 
 }  // extern "C"

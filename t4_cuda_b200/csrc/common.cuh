@@ -25,6 +25,11 @@ inline int check_launch() {
 // Streaming-multiprocessor count of the current device (cached per device).
 int sm_count();
 
+// TMA-streamed, SM-balanced W4A16 GEMV (gemv_w4_stream.cu).  Returns
+// T4B_ERR_UNSUPPORTED when the shape / alignment does not suit it.
+int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
+                   int K, int group, cudaStream_t stream);
+
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Division by a runtime constant d >= 1 for numerators n < 2^31:

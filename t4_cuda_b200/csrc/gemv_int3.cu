@@ -11,7 +11,7 @@
 //    kw0 + 2c + 1, i.e. 20 consecutive K, which is 5 MMAs of K = 16 per tile.
 //  * unpack_s3_exact (common.cuh) yields pairs (e_i, e_{i+5}); the activation
 //    fragment is permuted to the same pairs with PRMTs.
-//  * Any group size works.  When a word straddles a group boundary (group 128:
+//  * Any group size >= 10 works.  When a word straddles a group boundary (group 128:
 //    10*kw .. 10*kw+9 crosses a multiple of 128) each pair picks its scale and
 //    zero point per element; otherwise one scale serves the whole word.
 #include "common.cuh"
@@ -335,6 +335,8 @@ int dispatch_vec(const Int3Params& p, bool vec, int splits, cudaStream_t s) {
 int fused_int3(const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N, int K, int group,
                void* stream_) {
     if (M < 1 || N < 1 || K < 10 || (K % 10) != 0 || group < 1) return T4B_ERR_INVALID_VALUE;
+    // a 10-element word may straddle at most one group boundary
+    if (group < 10) return T4B_ERR_UNSUPPORTED;
     if (!A || !W || !S || !C) return T4B_ERR_NULL_POINTER;
     if (!aligned(A, 16) || !aligned(W, 4) || !aligned(S, 2) || !aligned(C, 2) || (Z && !aligned(Z, 2)))
         return T4B_ERR_MISALIGNED;

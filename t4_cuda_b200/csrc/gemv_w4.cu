@@ -25,6 +25,7 @@
 //    intended path for prefill shapes).
 #include "common.cuh"
 
+#include <atomic>
 #include <cooperative_groups.h>
 
 namespace cg = cooperative_groups;
@@ -35,6 +36,9 @@ namespace {
 constexpr int kWarps = 8;          // warps per CTA
 constexpr int kTileN = 64;         // output columns per CTA
 constexpr int kNB = 4;             // steps of loads kept in flight per lane
+constexpr int kStreamMaxM = 16;    // the streaming kernel serves one 16-row chunk
+
+std::atomic<int> g_gemv_kernel{T4B_GEMV_AUTO};
 
 struct GemvParams {
     const uint16_t* A;       // [M, K]
@@ -278,6 +282,10 @@ int fused_gemm(const void* A, const void* W, const void* S, const void* Z, void*
     if (!A || !W || !S || !C) return T4B_ERR_NULL_POINTER;
     if (!aligned(A, 16) || !aligned(W, 4) || !aligned(S, 2) || !aligned(C, 2) || (Z && !aligned(Z, 2)))
         return T4B_ERR_MISALIGNED;
+    if (g_gemv_kernel.load() == T4B_GEMV_AUTO && M <= kStreamMaxM) {
+        const int st = gemv_w4_stream(SIGNED, A, W, S, Z, C, M, N, K, group, static_cast<cudaStream_t>(stream_));
+        if (st != T4B_ERR_UNSUPPORTED) return st;
+    }
     GemvParams p;
     p.A = static_cast<const uint16_t*>(A);
     p.W = static_cast<const uint32_t*>(W);
@@ -308,6 +316,11 @@ int fused_gemm(const void* A, const void* W, const void* S, const void* Z, void*
 }  // namespace t4b
 
 extern "C" {
+
+int t4b_set_gemv_kernel(int which) {
+    if (which != T4B_GEMV_AUTO && which != T4B_GEMV_GENERIC) return -1;
+    return t4b::g_gemv_kernel.exchange(which);
+}
 
 int t4b_fused_w4a16_gemm_u4(const void* A, const void* W_packed, const void* scales, const void* zero_points,
                             void* C, int M, int N, int K, int group_size, void* stream) {

@@ -25,7 +25,31 @@ from . import _lib
 __all__ = [
     "dequantize_u4", "dequantize_s4", "dequantize_s3", "dequantize_fp8",
     "fused_w4a16_gemm_u4", "fused_w4a16_gemm_s4", "fused_h17_gemv_s3",
+    "set_gemv_kernel", "device_error",
 ]
+
+_GEMV_KERNELS = {"auto": 0, "generic": 1}
+
+
+def set_gemv_kernel(which="auto"):
+    """Choose the W4A16 matmul kernel process-wide: "auto" (TMA-streamed,
+    SM-balanced kernel wherever it applies) or "generic" (the register-streaming
+    kernel, for comparison).  Returns the previous choice."""
+    _check(which in _GEMV_KERNELS, f"which must be one of {sorted(_GEMV_KERNELS)}")
+    prev = _lib.load().t4b_set_gemv_kernel(_GEMV_KERNELS[which])
+    return {v: k for k, v in _GEMV_KERNELS.items()}[prev]
+
+
+def device_error(device=None, clear=True):
+    """Device error word of this library's workspace for the current stream of
+    ``device`` (0 = no kernel gave up a bounded wait).  Synchronizes the stream."""
+    import ctypes
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    out = ctypes.c_uint(0)
+    with _on_device(dev):
+        st = _lib.load().t4b_device_error(_stream_ptr(dev), ctypes.byref(out), 1 if clear else 0)
+    _lib.check(st, "t4b_device_error")
+    return out.value
 
 
 def _check(cond, msg):
@@ -235,7 +259,8 @@ def fused_h17_gemv_s3(A, W_packed, scales, zero_points, group_size=100):
     _check(M > 0 and N > 0 and K > 0, "Dimensions M, N, K must be positive")
     _check(K % 10 == 0, "K must be a multiple of 10 for H17 int3 packing")
     _check(W_packed.size(0) == K // 10, "W_packed first dim must equal K/10 (canonical H17 layout)")
-    _check(isinstance(group_size, int) and group_size >= 1, "group_size must be a positive int")
+    _check(isinstance(group_size, int) and group_size >= 10,
+           "group_size must be an int >= 10 (a 10-value word may straddle at most one group boundary)")
     num_groups = (K + group_size - 1) // group_size
     _check(scales.numel() == num_groups * N,
            f"scales must have num_groups * N elements (num_groups = ceil(K/{group_size}))")

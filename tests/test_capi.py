@@ -76,4 +76,5 @@ def test_gemm_argument_validation(lib):
     g = lib.t4b_fused_h17_gemv_s3
     assert g(p, p, p, None, p, 1, 64, 25, 100, None) == 1         # K % 10
     assert g(p, p, p, None, p, 1, 64, 200, 0, None) == 1          # group 0
+    assert g(p, p, p, None, p, 1, 64, 200, 7, None) == 4          # group < 10 unsupported
     assert g(p, None, p, None, p, 1, 64, 200, 100, None) == 2

@@ -56,7 +56,7 @@ def make_int3(rng, M, K, N, group, zp):
     (9, 100, 60, 100, True),         # N % 4 != 0, two m-tiles
     (16, 200, 128, 32, False),
     (2, 10, 8, 100, True),           # one word row; K % 4 != 0 activation path
-    (20, 1000, 72, 7, True),         # odd group size, M > 16
+    (20, 1000, 72, 13, True),        # odd group size, M > 16
 ])
 def test_int3_vs_oracle(cuda_device, M, K, N, group, zp):
     rng = np.random.default_rng(abs(hash((M, K, N, group, zp))) % 2 ** 32)
@@ -87,5 +87,8 @@ def test_checks_mirror_the_reference(cuda_device):
         t4_kernels.fused_h17_gemv_s3(A, W[:19], s, s)
     with pytest.raises(RuntimeError, match="num_groups"):
         t4_kernels.fused_h17_gemv_s3(A, W, s[:1], s[:1])
+    with pytest.raises(RuntimeError, match="group_size"):
+        t4_kernels.fused_h17_gemv_s3(A, W, torch.ones(29, 8, dtype=torch.float16, device=cuda_device), None,
+                                     group_size=7)
     with pytest.raises(RuntimeError, match="contiguous"):
         t4_kernels.fused_h17_gemv_s3(A, W.t().contiguous().t(), s, s)

@@ -31,7 +31,9 @@ enum {
     T4B_ERR_NULL_POINTER = 2,    /* a required pointer is NULL                          */
     T4B_ERR_MISALIGNED = 3,      /* a pointer breaks the alignment the op documents     */
     T4B_ERR_UNSUPPORTED = 4,     /* shape/option combination this build does not serve */
-    T4B_ERR_CUDA = 5             /* a CUDA runtime call or kernel launch failed         */
+    T4B_ERR_CUDA = 5,            /* a CUDA runtime call or kernel launch failed         */
+    T4B_ERR_SCRATCH_LIMIT = 6    /* problem needs more than the fixed scratch array of
+                                    t4b_fused_w4a16_gemv_noalloc                        */
 };
 
 /* Dequantization arithmetic (argument `mode` of the t4b_dequantize_* calls). */
@@ -111,6 +113,27 @@ int t4b_fused_w4a16_gemm_u4(const void* A, const void* W_packed, const void* sca
 int t4b_fused_w4a16_gemm_s4(const void* A, const void* W_packed, const void* scales,
                             const void* zero_points, void* C, int M, int N, int K,
                             int group_size, void* stream);
+
+/* Allocation-free decode GEMV.  No counterpart in the reference: an addition
+ * for callers that cannot allocate device memory while they run -- a serving
+ * engine that reserves all of HBM for its own pool at start-up, or a host
+ * runtime that forbids cudaMalloc once it is serving.  Same math and result as
+ * t4b_fused_w4a16_gemm_s4 (is_signed != 0) or _u4 (is_signed == 0) for
+ * M <= 16, but its scratch (split-tile partial sums, flags, an error word)
+ * lives in a fixed 4 MiB array inside this library, present on every GPU that
+ * loads it until the process exits; it never calls cudaMalloc or cudaFree.
+ * Extra requirements: M <= 16, N % 4 == 0, W_packed 16-byte and scales /
+ * zero_points 8-byte aligned, and (group_size / 8) a multiple of 8 or >= K / 8
+ * (else T4B_ERR_UNSUPPORTED); a shape whose partial sums do not fit in 4 MiB
+ * returns T4B_ERR_SCRATCH_LIMIT (Llama-3-8B projection shapes fit up to M = 16).
+ * The first call on each device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  Every call
+ * shares the one array: calls that overlap on the GPU (different streams,
+ * concurrent graph replays) race and give wrong results.  Each call clears the
+ * array's flags and error word on `stream` before its kernel. */
+int t4b_fused_w4a16_gemv_noalloc(const void* A, const void* W_packed, const void* scales,
+                                 const void* zero_points, void* C, int M, int N, int K,
+                                 int group_size, int is_signed, void* stream);
 
 /* ---- H17 fused INT3 GEMV ------------------------------------------------
  * C[M, N] (f16) = A[M, K] (f16) x dequant_s3(W)[K, N], W_packed int32 [K/10, N],

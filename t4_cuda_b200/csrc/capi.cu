@@ -133,6 +133,7 @@ const char* t4b_status_string(int status) {
         case T4B_ERR_MISALIGNED: return "a pointer is not aligned as the operation requires";
         case T4B_ERR_UNSUPPORTED: return "shape or option not supported by this build";
         case T4B_ERR_CUDA: return "CUDA runtime error (see t4b_last_cuda_error)";
+        case T4B_ERR_SCRATCH_LIMIT: return "problem too large for the fixed 4 MiB scratch of the allocation-free GEMV";
         default: return "unknown status";
     }
 }

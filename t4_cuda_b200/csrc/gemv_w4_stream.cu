@@ -33,6 +33,9 @@
 //   fp32 partial sums once per group; zero points enter through the
 //   activation sums (an extra MMA with an all-ones A fragment):
 //   y += s * (sum q a - z * sum a).
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 #include "tma.cuh"
 #include "workspace.h"
@@ -458,7 +461,7 @@ gemv_w4_stream_kernel(const __grid_constant__ CUtensorMap tmap, const StreamPara
 }
 
 template <int MT, bool SIGNED, bool HAS_ZP>
-int launch(const CUtensorMap& tmap, const StreamParams& p, int ychunks, cudaStream_t stream) {
+int launch(const CUtensorMap& tmap, const StreamParams& p, int ychunks, bool pdl, cudaStream_t stream) {
     constexpr int MR = 8 * MT;
     const size_t smem = 1024 + kStages * kStageBytes + (size_t)kWarps * kTileN * (MR + 1) * 4 + kStages * 8 +
                         kStages * 4 + 16;
@@ -478,16 +481,27 @@ int launch(const CUtensorMap& tmap, const StreamParams& p, int ychunks, cudaStre
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 1 : 0;
     cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tmap, p);
     if (err != cudaSuccess) return record_cuda_error(err);
     return T4B_OK;
 }
 
-}  // namespace
+int launch_any(bool is_signed, const CUtensorMap& tmap, const StreamParams& p, bool pdl, cudaStream_t stream) {
+    const int y = 1;
+    const bool zp = p.Z != nullptr;
+    if (p.M <= 8) {
+        if (is_signed) return zp ? launch<1, true, true>(tmap, p, y, pdl, stream) : launch<1, true, false>(tmap, p, y, pdl, stream);
+        return zp ? launch<1, false, true>(tmap, p, y, pdl, stream) : launch<1, false, false>(tmap, p, y, pdl, stream);
+    }
+    if (is_signed) return zp ? launch<2, true, true>(tmap, p, y, pdl, stream) : launch<2, true, false>(tmap, p, y, pdl, stream);
+    return zp ? launch<2, false, true>(tmap, p, y, pdl, stream) : launch<2, false, false>(tmap, p, y, pdl, stream);
+}
 
-int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
-                   int K, int group, cudaStream_t stream) {
+// Shape checks, tensor map and work split of one call.  The caller fills in
+// the scratch pointers (part, flags, err) before launching.
+int plan_stream(const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N, int K, int group,
+                CUtensorMap* tmap_out, StreamParams* out, size_t* flag_words, size_t* part_floats) {
     const int KW = K / 8;
     const int gw = group / 8;
     if ((N % 4) != 0 || !aligned(W, 16) || !aligned(S, 8) || (Z && !aligned(Z, 8))) return T4B_ERR_UNSUPPORTED;
@@ -496,16 +510,16 @@ int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, 
     // one row chunk only: the whole grid (one CTA per SM) must be resident,
     // because a split tile's reducer waits for the other segments' flags
     if (M > 16) return T4B_ERR_UNSUPPORTED;
-    CUtensorMap tmap;
-    if (!make_tmap_u32_2d(&tmap, W, (uint64_t)KW, (uint64_t)N, kChunkRows, kBoxCols)) return T4B_ERR_UNSUPPORTED;
-    const int MT = (M <= 8) ? 1 : 2;
-    const int MR = 8 * MT;
-    const int ychunks = 1;
+    if (!make_tmap_u32_2d(tmap_out, W, (uint64_t)KW, (uint64_t)N, kChunkRows, kBoxCols)) return T4B_ERR_UNSUPPORTED;
+    const int MR = (M <= 8) ? 8 : 16;
     StreamParams p;
     p.A = static_cast<const uint16_t*>(A);
     p.S = static_cast<const uint16_t*>(S);
     p.Z = static_cast<const uint16_t*>(Z);
     p.C = static_cast<uint16_t*>(C);
+    p.part = nullptr;
+    p.flags = nullptr;
+    p.err = nullptr;
     p.M = M; p.N = N; p.K = K; p.KW = KW;
     p.tiles = (N + kTileN - 1) / kTileN;
     p.cpt = (KW + kChunkRows - 1) / kChunkRows;
@@ -523,20 +537,98 @@ int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, 
         if (n > max_segs) max_segs = n;
     }
     p.max_segs = max_segs;
-    const size_t part_floats = (size_t)p.tiles * max_segs * kTileN * MR;
-    const size_t flag_words = (size_t)p.tiles * max_segs;
+    *part_floats = (size_t)p.tiles * max_segs * kTileN * MR;
+    *flag_words = (size_t)p.tiles * max_segs;
+    *out = p;
+    return T4B_OK;
+}
+
+}  // namespace
+
+int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
+                   int K, int group, cudaStream_t stream) {
+    CUtensorMap tmap;
+    StreamParams p;
+    size_t flag_words = 0, part_floats = 0;
+    int st = plan_stream(A, W, S, Z, C, M, N, K, group, &tmap, &p, &flag_words, &part_floats);
+    if (st != T4B_OK) return st;
     Workspace ws;
-    const int st = acquire_workspace(stream, flag_words, part_floats, &ws);
+    st = acquire_workspace(stream, flag_words, part_floats, &ws);
     if (st != T4B_OK) return st;
     p.part = ws.part;
     p.flags = ws.counters;
     p.err = ws.error;
-    if (MT == 1) {
-        if (is_signed) return Z ? launch<1, true, true>(tmap, p, ychunks, stream) : launch<1, true, false>(tmap, p, ychunks, stream);
-        return Z ? launch<1, false, true>(tmap, p, ychunks, stream) : launch<1, false, false>(tmap, p, ychunks, stream);
+    return launch_any(is_signed, tmap, p, /*pdl=*/true, stream);
+}
+
+// ---- allocation-free variant ----------------------------------------------
+// Some callers cannot allocate device memory while they run: an inference
+// server that reserves all of HBM for its own pool up front and hands it out
+// itself, a runtime that forbids allocation once serving has started, or code
+// that must not touch the allocator at all.  For them the decode GEMV above
+// can run on a fixed scratch array that is part of this library's image on
+// every GPU that loads it (kept until the process exits), instead of the
+// per-stream workspace the library would otherwise cudaMalloc.
+//
+// Layout of the array: bytes [0, 256) hold the device error word, then the
+// per-segment "published" flags, then (at a 256-byte boundary) the partial
+// sums of split tiles.  Each call clears the error word and the flags with
+// one cudaMemsetAsync; the partials need no clearing (every one is written
+// before it is read).  All calls share the array, so two calls that overlap
+// on the GPU (different streams, or concurrent graph replays) race.
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;   // 4 MiB
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device.  The host-side
+// name of the array is only a stand-in; the address has to be looked up once
+// per device, with that device current.
+int static_scratch_address(unsigned char** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    static std::mutex mu;
+    static std::vector<unsigned char*> addr;
+    std::lock_guard<std::mutex> lock(mu);
+    if ((size_t)dev >= addr.size()) addr.resize(dev + 1, nullptr);
+    if (!addr[dev]) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        addr[dev] = static_cast<unsigned char*>(ptr);
     }
-    if (is_signed) return Z ? launch<2, true, true>(tmap, p, ychunks, stream) : launch<2, true, false>(tmap, p, ychunks, stream);
-    return Z ? launch<2, false, true>(tmap, p, ychunks, stream) : launch<2, false, false>(tmap, p, ychunks, stream);
+    *out = addr[dev];
+    return T4B_OK;
 }
 
 }  // namespace t4b
+
+extern "C" int t4b_fused_w4a16_gemv_noalloc(const void* A, const void* W_packed, const void* scales,
+                                            const void* zero_points, void* C, int M, int N, int K, int group_size,
+                                            int is_signed, void* stream_) {
+    using namespace t4b;
+    if (M < 1 || N < 1 || K < 8 || (K % 8) != 0) return T4B_ERR_INVALID_VALUE;
+    if (group_size < 8 || (group_size % 8) != 0 || (K % group_size) != 0) return T4B_ERR_INVALID_VALUE;
+    if (!A || !W_packed || !scales || !C) return T4B_ERR_NULL_POINTER;
+    if (!aligned(A, 16) || !aligned(W_packed, 4) || !aligned(scales, 2) || !aligned(C, 2) ||
+        (zero_points && !aligned(zero_points, 2)))
+        return T4B_ERR_MISALIGNED;
+    const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    CUtensorMap tmap;
+    StreamParams p;
+    size_t flag_words = 0, part_floats = 0;
+    int st = plan_stream(A, W_packed, scales, zero_points, C, M, N, K, group_size, &tmap, &p, &flag_words,
+                         &part_floats);
+    if (st != T4B_OK) return st;
+    const size_t head = 256 + flag_words * sizeof(unsigned);
+    const size_t part_off = (head + 255) & ~size_t(255);
+    if (part_off + part_floats * sizeof(float) > kStaticScratchBytes) return T4B_ERR_SCRATCH_LIMIT;
+    unsigned char* base = nullptr;
+    st = static_scratch_address(&base);
+    if (st != T4B_OK) return st;
+    cudaError_t e = cudaMemsetAsync(base, 0, head, stream);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    p.err = reinterpret_cast<unsigned*>(base);
+    p.flags = reinterpret_cast<unsigned*>(base + 256);
+    p.part = reinterpret_cast<float*>(base + part_off);
+    return launch_any(is_signed != 0, tmap, p, /*pdl=*/false, stream);
+}

@@ -39,7 +39,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_status_strings_and_version(lib):
     assert lib.t4b_status_string(0) == b"ok"
-    for code in range(1, 6):
+    for code in range(1, 7):
         assert lib.t4b_status_string(code) and lib.t4b_status_string(code) != b"unknown status"
     assert lib.t4b_version() >> 16 == 1
     assert lib.t4b_last_cuda_error() == 0
@@ -78,3 +78,14 @@ def test_gemm_argument_validation(lib):
     assert g(p, p, p, None, p, 1, 64, 200, 0, None) == 1          # group 0
     assert g(p, p, p, None, p, 1, 64, 200, 7, None) == 4          # group < 10 unsupported
     assert g(p, None, p, None, p, 1, 64, 200, 100, None) == 2
+
+
+def test_noalloc_gemv_argument_validation(lib):
+    p = _fake()
+    f = lib.t4b_fused_w4a16_gemv_noalloc
+    assert f(p, p, p, None, p, 0, 64, 64, 64, 1, None) == 1       # M = 0
+    assert f(p, p, p, None, p, 1, 64, 60, 60, 1, None) == 1       # K % 8
+    assert f(None, p, p, None, p, 1, 64, 64, 64, 1, None) == 2
+    assert f(_fake(0x10008), p, p, None, p, 1, 64, 64, 64, 0, None) == 3   # A must be 16-byte aligned
+    assert f(p, p, p, None, p, 17, 64, 64, 64, 1, None) == 4      # M > 16 is not a decode shape
+    assert f(p, p, p, None, p, 1, 62, 64, 64, 1, None) == 4       # N % 4

@@ -121,6 +121,32 @@ bool make_tmap_f16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
     return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, rows, cols, box_rows, box_cols);
 }
 
+bool make_tmap_2d_ex(CUtensorMap* map, bool fp16, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                     uint32_t box_cols, int swizzle_bytes, int l2_promotion_bytes) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const uint32_t esize = fp16 ? 2 : 4;
+    if ((cols * esize) % 16 != 0 || (reinterpret_cast<uintptr_t>(base) % 16) != 0) return false;
+    if ((box_cols * esize) % 16 != 0) return false;
+    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+    if (swizzle_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
+    else if (swizzle_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
+    else if (swizzle_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    else if (swizzle_bytes != 0) return false;
+    if (swizzle_bytes && box_cols * esize > (uint32_t)swizzle_bytes) return false;
+    CUtensorMapL2promotion l2 = CU_TENSOR_MAP_L2_PROMOTION_NONE;
+    if (l2_promotion_bytes == 64) l2 = CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
+    else if (l2_promotion_bytes == 128) l2 = CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
+    else if (l2_promotion_bytes == 256) l2 = CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * esize};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 2,
+              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, l2,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace t4b
 
 extern "C" {

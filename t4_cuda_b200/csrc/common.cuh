@@ -30,6 +30,11 @@ int sm_count();
 int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
                    int K, int group, cudaStream_t stream);
 
+// Decode GEMV with resident activations (M <= 16, M * K <= 32768); returns
+// T4B_ERR_UNSUPPORTED (without launching) for shapes it does not take.
+int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
+                   int K, int group, cudaStream_t stream);
+
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Division by a runtime constant d >= 1 for numerators n < 2^31:

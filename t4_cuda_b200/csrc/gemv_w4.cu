@@ -282,7 +282,12 @@ int fused_gemm(const void* A, const void* W, const void* S, const void* Z, void*
     if (!A || !W || !S || !C) return T4B_ERR_NULL_POINTER;
     if (!aligned(A, 16) || !aligned(W, 4) || !aligned(S, 2) || !aligned(C, 2) || (Z && !aligned(Z, 2)))
         return T4B_ERR_MISALIGNED;
-    if (g_gemv_kernel.load() == T4B_GEMV_AUTO && M <= kStreamMaxM) {
+    const int choice = g_gemv_kernel.load();
+    if (choice == T4B_GEMV_AUTO && M <= kStreamMaxM) {
+        const int st = gemv_w4_decode(SIGNED, A, W, S, Z, C, M, N, K, group, static_cast<cudaStream_t>(stream_));
+        if (st != T4B_ERR_UNSUPPORTED) return st;
+    }
+    if ((choice == T4B_GEMV_AUTO || choice == T4B_GEMV_STREAM) && M <= kStreamMaxM) {
         const int st = gemv_w4_stream(SIGNED, A, W, S, Z, C, M, N, K, group, static_cast<cudaStream_t>(stream_));
         if (st != T4B_ERR_UNSUPPORTED) return st;
     }
@@ -318,7 +323,7 @@ int fused_gemm(const void* A, const void* W, const void* S, const void* Z, void*
 extern "C" {
 
 int t4b_set_gemv_kernel(int which) {
-    if (which != T4B_GEMV_AUTO && which != T4B_GEMV_GENERIC) return -1;
+    if (which != T4B_GEMV_AUTO && which != T4B_GEMV_GENERIC && which != T4B_GEMV_STREAM) return -1;
     return t4b::g_gemv_kernel.exchange(which);
 }
 

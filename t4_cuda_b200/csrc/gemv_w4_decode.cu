@@ -1,0 +1,642 @@
+// Decode W4A16 GEMV with the activations resident in shared memory:
+//
+//   C[M, N] = A[M, K] x dequant(W)[K, N],  W int32 [K/8, N], group scales [K/g, N]
+//
+// for M <= 16 and M * K <= 32768 (one token, or a handful, per call).
+//
+// Work decomposition
+//   Output columns are cut into 16-column tiles.  CTA b of G (G <= SMs) owns
+//   the contiguous tiles [b T / G, (b+1) T / G) over the whole of K, so no two
+//   CTAs ever produce the same output: there is no cross-CTA traffic and no
+//   wait on another CTA.  A CTA walks its tiles in groups of up to four
+//   (64 columns); each group streams its weight columns over K through a
+//   ring of shared-memory stages and ends with one reduction across warps.
+//
+// Stages
+//   A CTA has WARPS warps (16 for M <= 8, else 8) and a stage gives each warp
+//   16 word rows x 32 columns: one TMA box per 16-column tile of the group,
+//   covering all the stage's rows (8 * WARPS rows for groups of 3-4 tiles,
+//   16 * WARPS rows for groups of 1-2; 64-byte swizzle), plus one box of
+//   group scales (and one of zero points) over the stage's rows and the
+//   group's 64 or 32 columns -- a handful of large copies per stage, because the
+//   thread that issues a copy stalls while the SM's copy engine is busy.
+//   All of it is constant data, so the first stages are issued at kernel
+//   entry, before griddepcontrol.wait, and stream in while the previous
+//   kernel in the stream drains (two CTAs fit on an SM: one computing, one
+//   prefetching).  Whichever warp finishes a stage last refills its slot.
+//
+// Activations
+//   After griddepcontrol.wait the CTA copies A into shared memory once, as one
+//   16-byte record (a0,a4),(a1,a5),(a2,a6),(a3,a7) per batch row and 8-element
+//   word row -- exactly the B fragment of mma.m16n8k16 that the unpacked
+//   weights below need -- and sums every batch row over each flush block of 8
+//   or 16 word rows.
+//
+// Math
+//   Warp (wc, rb) owns 32 columns (two 16-column boxes) x 16 word rows of a
+//   stage.  A lane reads four words of one row (one 16-byte load) and turns
+//   each into four fp16x2 registers with one LOP3 per nibble pair (0,4),
+//   (1,5), (2,6), (3,7): the pair lands in mantissa bits 4-7 under exponent
+//   2^6, which reads exactly as 64 + u (unsigned) or, with the nibble's top
+//   bit flipped, 72 + s (signed).  These offset integers are the A operand of
+//   mma.m16n8k16 with fp32 accumulation; per flush block the offset leaves
+//   with the activation sum:
+//       y += scale * (sum (o + q) a  -  (o + z) sum a),   o = 64 or 72.
+#include <algorithm>
+
+#include "common.cuh"
+#include "tma.cuh"
+#include "workspace.h"
+
+namespace t4b {
+namespace {
+
+constexpr int kBoxCols = 16;                       // columns per TMA box (64 bytes)
+constexpr int kMaxStages = 12;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr unsigned kErrTimeout = 1u;
+
+template <int MT>
+struct Shape {
+    static constexpr int kWarps = (MT == 1) ? 16 : 8;
+    static constexpr int kThreads = 32 * kWarps;
+    static constexpr int kWeightBytes = kWarps * 2048;         // packed words per stage
+    static constexpr int kRowsNarrow = 16 * kWarps;            // stage rows, 1 warp column (1-2 tiles)
+    static constexpr int kRowsWide = 8 * kWarps;               // stage rows, 2 warp columns (3-4 tiles)
+};
+
+struct DecodeParams {
+    const uint16_t* A;
+    uint16_t* C;
+    unsigned* err;
+    int M, N, K, KW;
+    int KWp;            // word rows padded to a multiple of the narrow stage (resident activations)
+    int T, G;           // 16-column tiles, CTAs
+    int gw;             // group size in word rows
+    int gw_shift;       // log2(gw) when gw is a power of two (it then divides any stage it is smaller than)
+    int fb;             // flush block in word rows: 8 (gw == 8) or 16
+    int sbr_wide;       // scale rows of a wide stage's scale box: rows_wide / gw, or 1 when gw >= rows_wide
+    int sbr_narrow;     // same for a narrow stage
+    int s_bytes;        // bytes of the scale (and of the zero-point) region of a slot
+    int stages;         // ring depth
+    int early;          // stages issued before griddepcontrol.wait (the rest right after it)
+    int slot_bytes;     // bytes of one ring slot
+    int s_wide, s_narrow;   // stages of a tile group with 2 / 1 warp columns
+    int act_bytes;      // resident activation records (bytes)
+    int sum_floats;     // flush-block activation sums
+    int red_floats;     // cross-warp reduction buffer
+    FastDiv kwdiv;      // division by KWp
+};
+
+struct DecodeMaps {
+    CUtensorMap w_wide;     // packed words, box 16 columns x rows_wide
+    CUtensorMap w_narrow;   // packed words, box 16 columns x rows_narrow
+    CUtensorMap s_wide;     // scales, box 64 columns x sbr_wide rows
+    CUtensorMap s_narrow;   // scales, box 32 columns x sbr_narrow rows
+    CUtensorMap z_wide;     // zero points, same boxes (unused without them)
+    CUtensorMap z_narrow;
+};
+
+// A pure function of its operands (not volatile), so the compiler may
+// interleave independent MMAs with the loads and unpacking around them.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Same with a zero accumulator in (the first MMA of a flush block).
+__device__ __forceinline__ void mma_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    const float z = 0.f;
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+// Shared-memory loads by 32-bit address.  Not volatile (free to interleave
+// with the math), but with a memory clobber so they stay after the mbarrier
+// wait that makes the data visible.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+    return v;
+}
+
+// Nibble pairs (0,4), (1,5), (2,6), (3,7) of w as fp16x2 offset integers:
+// 64 + u (unsigned) or 72 + s (signed two's complement nibble).
+template <bool SIGNED>
+__device__ __forceinline__ void unpack_offset64(uint32_t w, uint32_t (&e)[4]) {
+    constexpr uint32_t kMask = 0x00F000F0u;
+    constexpr uint32_t kMagic = SIGNED ? 0x54805480u : 0x54005400u;
+    constexpr int kLut = SIGNED ? 0x6A : 0xEA;     // (a & b) ^ c  /  (a & b) | c
+    e[0] = lop3<kLut>(w << 4, kMask, kMagic);
+    e[1] = lop3<kLut>(w, kMask, kMagic);
+    e[2] = lop3<kLut>(w >> 4, kMask, kMagic);
+    e[3] = lop3<kLut>(w >> 8, kMask, kMagic);
+}
+
+// Word-row offset (0..15) of lane column c in row step j of a warp's 16 rows;
+// with the 64-byte swizzle this makes every quarter-warp read hit 8 distinct
+// bank groups (a row step is 4 rows read by the 4 lane columns).
+__device__ __forceinline__ int row_of(int j, int c) { return (c & 1) + 4 * (c >> 1) + 2 * (j & 1) + 8 * (j >> 1); }
+
+struct CtaPlan {
+    int t0, ng, nt_last, s_last, total;
+};
+
+template <int MT>
+__device__ __forceinline__ CtaPlan cta_plan(const DecodeParams& p) {
+    CtaPlan q;
+    const uint32_t b = blockIdx.x;
+    q.t0 = (int)(b * (uint32_t)p.T / (uint32_t)p.G);          // b * T < 2^32 (checked on the host)
+    const int t1 = (int)((b + 1) * (uint32_t)p.T / (uint32_t)p.G);
+    const int n = t1 - q.t0;
+    q.ng = (n + 3) >> 2;
+    q.nt_last = n - 4 * (q.ng - 1);
+    q.s_last = (q.nt_last > 2) ? p.s_wide : p.s_narrow;
+    q.total = (q.ng - 1) * p.s_wide + q.s_last;
+    return q;
+}
+
+// Issue ring stage i (global stage index within this CTA) into `slot`.
+template <int MT, bool HAS_ZP>
+__device__ __forceinline__ void issue_stage(const DecodeParams& p, const CtaPlan& q, const DecodeMaps& maps,
+                                            uint8_t* ring, uint64_t* full, int i, int slot) {
+    using S = Shape<MT>;
+    const int full_stages = (q.ng - 1) * p.s_wide;
+    int g, ks;
+    if (i < full_stages) {
+        g = i / p.s_wide;
+        ks = i - g * p.s_wide;
+    } else {
+        g = q.ng - 1;
+        ks = i - full_stages;
+    }
+    const int nt = (g < q.ng - 1) ? 4 : q.nt_last;
+    const bool wide = nt > 2;
+    const int rows = wide ? S::kRowsWide : S::kRowsNarrow;
+    const int row0 = ks * rows;
+    const int tg0 = q.t0 + 4 * g;
+    const uint32_t sbox = wide ? (uint32_t)p.sbr_wide * 128 : (uint32_t)p.sbr_narrow * 64;
+    mbar_arrive_expect_tx(&full[slot], (uint32_t)(nt * rows * 64) + sbox * (HAS_ZP ? 2 : 1));
+    uint8_t* base = ring + (size_t)slot * p.slot_bytes;
+    const CUtensorMap* tw = wide ? &maps.w_wide : &maps.w_narrow;
+    for (int bx = 0; bx < nt; ++bx) tma_load_2d(base + bx * rows * 64, tw, kBoxCols * (tg0 + bx), row0, &full[slot]);
+    const int sr = (p.gw_shift >= 0) ? (row0 >> p.gw_shift) : row0 / p.gw;
+    uint8_t* sbase = base + S::kWeightBytes;
+    tma_load_2d(sbase, wide ? &maps.s_wide : &maps.s_narrow, kBoxCols * tg0, sr, &full[slot]);
+    if constexpr (HAS_ZP) tma_load_2d(sbase + p.s_bytes, wide ? &maps.z_wide : &maps.z_narrow, kBoxCols * tg0, sr, &full[slot]);
+}
+
+// acc += s * (dg + o * sum a) for the two 16-column sub-tiles of this lane,
+// o = -(offset + z).  s / z: the lane's four columns 4L..4L+3.
+template <int MT, bool SIGNED, bool HAS_ZP>
+__device__ __forceinline__ void flush(float (&acc)[MT][2][4], const float (&dg)[MT][2][4], uint32_t saddr,
+                                      uint32_t zaddr, uint32_t sum_addr) {
+    constexpr float kOff = SIGNED ? 72.f : 64.f;
+    const uint2 sv = lds64(saddr);
+    float s[4] = {h_to_f((uint16_t)(sv.x & 0xFFFF)), h_to_f((uint16_t)(sv.x >> 16)),
+                  h_to_f((uint16_t)(sv.y & 0xFFFF)), h_to_f((uint16_t)(sv.y >> 16))};
+    float o[4] = {-kOff, -kOff, -kOff, -kOff};
+    if constexpr (HAS_ZP) {
+        const uint2 zv = lds64(zaddr);
+        o[0] = -(kOff + h_to_f((uint16_t)(zv.x & 0xFFFF)));
+        o[1] = -(kOff + h_to_f((uint16_t)(zv.x >> 16)));
+        o[2] = -(kOff + h_to_f((uint16_t)(zv.y & 0xFFFF)));
+        o[3] = -(kOff + h_to_f((uint16_t)(zv.y >> 16)));
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        const uint2 sv2 = lds64(sum_addr + 32 * mt);
+        const float sa[2] = {__uint_as_float(sv2.x), __uint_as_float(sv2.y)};
+#pragma unroll
+        for (int X = 0; X < 2; ++X)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int k = 2 * X + (e >> 1);
+                acc[mt][X][e] = fmaf(s[k], fmaf(o[k], sa[e & 1], dg[mt][X][e]), acc[mt][X][e]);
+            }
+    }
+}
+
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8>
+__global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
+gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p) {
+    using S = Shape<MT>;
+    constexpr int kWarps = S::kWarps;
+    constexpr int kThreads = S::kThreads;
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte aligned ring (pointer arithmetic on smem_raw keeps the
+    // compiler aware that every access below is to shared memory)
+    uint8_t* ring = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint8_t* act = ring + (size_t)p.stages * p.slot_bytes;
+    float* sums = reinterpret_cast<float*>(act + p.act_bytes);
+    float* red = sums + p.sum_floats;
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + p.red_floats);
+    int* readers = reinterpret_cast<int*>(full + kMaxStages);
+    volatile int* sflag = reinterpret_cast<volatile int*>(readers + kMaxStages);   // [0] abort, [1] stages issued
+
+    pdl_launch_dependents();
+    const CtaPlan q = cta_plan<MT>(p);
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            readers[s] = 0;
+        }
+        sflag[0] = 0;
+        fence_barrier_init();
+        prefetch_tmap(&maps.w_wide);
+        prefetch_tmap(&maps.w_narrow);
+        prefetch_tmap(&maps.s_wide);
+        prefetch_tmap(&maps.s_narrow);
+        if constexpr (HAS_ZP) {
+            prefetch_tmap(&maps.z_wide);
+            prefetch_tmap(&maps.z_narrow);
+        }
+        // weights, scales and zero points are never written by a kernel of
+        // this library, so they may be fetched before the previous kernel ends
+        const int early = q.total < p.early ? q.total : p.early;
+        for (int s = 0; s < early; ++s) issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, s, s);
+        sflag[1] = early;
+    }
+    pdl_wait_prior_grid();     // A and C may belong to the previous kernel
+
+    // ---- resident activations: permuted records + flush-block sums.  Every
+    // thread issues kPrep independent loads before using any, so the prologue
+    // costs one L2 round trip per batch, not one per record.
+    {
+        constexpr int kPrep = 4;
+        const int MB = 8 * MT;
+        const int items = p.M * p.KWp;      // a multiple of 128: every test below is uniform per warp
+        const uint32_t pitch = (uint32_t)(p.KWp + 2);
+        for (int base = 0; base < items; base += kThreads * kPrep) {
+            uint4 v[kPrep];
+#pragma unroll
+            for (int k = 0; k < kPrep; ++k) {
+                const int it = base + k * kThreads + tid;
+                const int m = (int)fdiv((uint32_t)it, p.kwdiv);
+                const int kw = it - m * p.KWp;
+                v[k] = make_uint4(0, 0, 0, 0);
+                if (it < items && kw < p.KW)
+                    v[k] = __ldcg(reinterpret_cast<const uint4*>(p.A + (size_t)m * p.K + 8 * (size_t)kw));
+            }
+#pragma unroll
+            for (int k = 0; k < kPrep; ++k) {
+                const int it = base + k * kThreads + tid;
+                if (it >= items) continue;      // uniform per warp (the shuffles below need all 32 lanes)
+                const int m = (int)fdiv((uint32_t)it, p.kwdiv);
+                const int kw = it - m * p.KWp;
+                uint4 rec;
+                rec.x = prmt(v[k].x, v[k].z, 0x5410);
+                rec.y = prmt(v[k].x, v[k].z, 0x7632);
+                rec.z = prmt(v[k].y, v[k].w, 0x5410);
+                rec.w = prmt(v[k].y, v[k].w, 0x7632);
+                *reinterpret_cast<uint4*>(act + ((size_t)m * pitch + kw) * 16) = rec;
+                const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&v[k].x));
+                const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&v[k].y));
+                const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&v[k].z));
+                const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&v[k].w));
+                float s = ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                s += __shfl_xor_sync(0xffffffffu, s, 4);
+                if (p.fb == 16) s += __shfl_xor_sync(0xffffffffu, s, 8);
+                if ((kw & (p.fb - 1)) == 0) sums[(kw / p.fb) * MB + m] = s;
+            }
+        }
+        for (int idx = tid; idx < p.sum_floats; idx += kThreads)
+            if ((idx & (MB - 1)) >= p.M) sums[idx] = 0.f;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        // The rest of the ring, issued only now: the activation loads above
+        // were on the critical path and should not have queued behind this
+        // SM's weight stream (and an issue that stalls on a busy copy engine
+        // no longer holds up the whole CTA).
+        const int first = q.total < p.stages ? q.total : p.stages;
+        for (int s = sflag[1]; s < first; ++s) issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, s, s);
+        sflag[1] = first;
+    }
+
+    const int warp = tid >> 5, lane = tid & 31;
+    const int r = lane >> 2, c = lane & 3;
+    const int bb = r & 1;                     // which of the warp's two boxes
+    const int L = (r >> 1) ^ (r & 1);         // 16-byte chunk (4 columns) of that box
+    const uint32_t ring_a = smem_addr(ring);
+    const uint32_t act_a = smem_addr(act);
+    const uint32_t sum_lane = smem_addr(sums) + (uint32_t)(2 * c) * 4;
+    const uint32_t pitch16 = (uint32_t)(p.KWp + 2) * 16;
+    constexpr bool fb8 = FB8;     // 8-row flush blocks (group 64), else 16
+
+    float acc[MT][2][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int X = 0; X < 2; ++X)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][X][e] = 0.f;
+
+    bool aborted = false;
+    int i = 0, slot = 0;
+    uint32_t phase = 0;
+    for (int g = 0; g < q.ng; ++g) {
+        const int nt = (g < q.ng - 1) ? 4 : q.nt_last;
+        const int nwc = (nt + 1) >> 1;            // warp columns (32 columns each)
+        const int rbs = kWarps / nwc;             // 16-row blocks per stage
+        const int rows = 16 * rbs;
+        const int nst = (nwc == 2) ? p.s_wide : p.s_narrow;
+        const int wc = (nwc == 2) ? warp / (kWarps / 2) : 0;
+        const int rb = warp - wc * rbs;           // 16-row block of the stage
+        // Loads below are unconditional (a guard around inline asm becomes a
+        // branch that splits the stage into small scheduling regions).  A
+        // lane whose box lies past the group's last tile reads another box of
+        // the slot, and a lane past the last batch row reads row M-1: both
+        // only feed MMA rows / columns that are never stored.
+        const int box = 2 * wc + bb;
+        const int kw_lane = 16 * rb;              // first word row of this warp in a stage
+        uint32_t woff[4], aoff[MT][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int row = kw_lane + row_of(j, c);
+            woff[j] = (uint32_t)(box * rows * 64 + row * 64) + (uint32_t)((L ^ ((row >> 1) & 3)) << 4);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const int m = min(r + 8 * mt, p.M - 1);
+                aoff[mt][j] = act_a + (uint32_t)m * pitch16 + (uint32_t)row * 16;
+            }
+        }
+        // scale row of this warp's flush blocks (rows kw_lane + 8h of the stage);
+        // a scale box row holds the group's 64 (wide) or 32 (narrow) columns
+        const int srow_bytes = (nwc == 2) ? 128 : 64;
+        const bool per_row = p.gw_shift >= 0 && p.gw < rows;
+        uint32_t soff[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int srow = per_row ? ((kw_lane + 8 * h) >> p.gw_shift) : 0;
+            soff[h] = (uint32_t)(S::kWeightBytes + srow * srow_bytes + (16 * box + 4 * L) * 2);
+        }
+        const uint32_t zdelta = (uint32_t)p.s_bytes;
+
+        for (int ks = 0; ks < nst; ++ks, ++i) {
+            if (!aborted && !mbar_wait_bounded(&full[slot], phase, kWaitLimitNs)) {
+                aborted = true;
+                sflag[0] = 1;
+                atomicOr(p.err, kErrTimeout);
+            }
+            if (!aborted) {
+                const uint32_t st = ring_a + (uint32_t)slot * p.slot_bytes;
+                const int row0 = ks * rows;
+                const uint32_t arow = (uint32_t)row0 * 16;
+                float dg[MT][2][4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint4 wv = lds128(st + woff[j]);
+                    uint4 av[MT];
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) av[mt] = lds128(aoff[mt][j] + arow);
+                    uint32_t e0[4], e1[4], e2[4], e3[4];
+                    unpack_offset64<SIGNED>(wv.x, e0);   // column 4L     (sub-tile 0, MMA row r)
+                    unpack_offset64<SIGNED>(wv.y, e1);   // column 4L + 1 (sub-tile 0, MMA row r + 8)
+                    unpack_offset64<SIGNED>(wv.z, e2);   // column 4L + 2 (sub-tile 1, MMA row r)
+                    unpack_offset64<SIGNED>(wv.w, e3);   // column 4L + 3 (sub-tile 1, MMA row r + 8)
+                    const bool first = (j == 0) || (j == 2 && fb8);
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        if (first) {
+                            mma_16816_zero(dg[mt][0], e0[0], e1[0], e0[1], e1[1], av[mt].x, av[mt].y);
+                            mma_16816_zero(dg[mt][1], e2[0], e3[0], e2[1], e3[1], av[mt].x, av[mt].y);
+                        } else {
+                            mma_16816(dg[mt][0], e0[0], e1[0], e0[1], e1[1], av[mt].x, av[mt].y);
+                            mma_16816(dg[mt][1], e2[0], e3[0], e2[1], e3[1], av[mt].x, av[mt].y);
+                        }
+                        mma_16816(dg[mt][0], e0[2], e1[2], e0[3], e1[3], av[mt].z, av[mt].w);
+                        mma_16816(dg[mt][1], e2[2], e3[2], e2[3], e3[3], av[mt].z, av[mt].w);
+                    }
+                    if (j == 1 && fb8) {
+                        const uint32_t b8 = (uint32_t)((row0 + kw_lane) >> 3);
+                        flush<MT, SIGNED, HAS_ZP>(acc, dg, st + soff[0], st + soff[0] + zdelta,
+                                                  sum_lane + b8 * (32 * MT));
+                    }
+                }
+                if (fb8) {
+                    const uint32_t b8 = (uint32_t)((row0 + kw_lane) >> 3) + 1;
+                    flush<MT, SIGNED, HAS_ZP>(acc, dg, st + soff[1], st + soff[1] + zdelta,
+                                              sum_lane + b8 * (32 * MT));
+                } else {
+                    const uint32_t b16 = (uint32_t)((row0 + kw_lane) >> 4);
+                    flush<MT, SIGNED, HAS_ZP>(acc, dg, st + soff[0], st + soff[0] + zdelta,
+                                              sum_lane + b16 * (32 * MT));
+                }
+            }
+            // Every lane's reads of this slot are complete (their results fed
+            // the MMAs above); the last warp to get here refills the slot.
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();   // this warp's reads of the slot before the count (release)
+                if (atomicAdd(&readers[slot], 1) == kWarps - 1) {
+                    readers[slot] = 0;
+                    const int nxt = i + p.stages;
+                    if (nxt < q.total && !sflag[0]) {
+                        fence_proxy_async_smem();
+                        issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, nxt, slot);
+                        sflag[1] = nxt + 1;
+                    }
+                }
+            }
+            if (++slot == p.stages) {
+                slot = 0;
+                phase ^= 1u;
+            }
+        }
+
+        // ---- group done: sum the row blocks of each warp column in a fixed order
+        const int M = p.M;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int X = 0; X < 2; ++X)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int col = 16 * bb + 4 * L + 2 * X + (e >> 1);
+                    const int m = 8 * mt + 2 * c + (e & 1);
+                    if (m < M) red[(warp * 32 + col) * M + m] = acc[mt][X][e];
+                    acc[mt][X][e] = 0.f;
+                }
+        __syncthreads();
+        const int col_base = kBoxCols * (q.t0 + 4 * g);
+        int ncols = kBoxCols * nt;
+        if (col_base + ncols > p.N) ncols = p.N - col_base;
+        for (int pair = warp; pair < nwc * M; pair += kWarps) {
+            const int w = pair / M, m = pair - w * M;
+            const int col = 32 * w + lane;
+            if (col < ncols) {
+                float v = 0.f;
+                for (int k = 0; k < rbs; ++k) v += red[((w * rbs + k) * 32 + lane) * M + m];
+                p.C[(size_t)m * p.N + col_base + col] = __half_as_ushort(__float2half_rn(v));
+            }
+        }
+        __syncthreads();
+    }
+
+    if (aborted && tid == 0) {
+        // do not leave while copies may still be landing in this CTA's memory
+        const int issued = sflag[1];
+        for (int j = (issued > p.stages ? issued - p.stages : 0); j < issued; ++j)
+            mbar_wait_bounded(&full[j % p.stages], (uint32_t)((j / p.stages) & 1), kWaitLimitNs / 4);
+    }
+}
+
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8>
+int launch(const DecodeMaps& maps, const DecodeParams& p, size_t smem,
+           cudaStream_t stream) {
+    auto kern = gemv_w4_decode_kernel<MT, SIGNED, HAS_ZP, FB8>;
+    static int configured = 0;   // largest dynamic shared memory set so far for this instantiation
+    if ((int)smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        configured = (int)smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.G, 1, 1);
+    cfg.blockDim = dim3(Shape<MT>::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, maps, p);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    return T4B_OK;
+}
+
+template <int MT, bool SIGNED>
+int dispatch_zp(bool zp, bool fb8, const DecodeMaps& maps, const DecodeParams& p, size_t smem,
+                cudaStream_t stream) {
+    if (zp) return fb8 ? launch<MT, SIGNED, true, true>(maps, p, smem, stream)
+                       : launch<MT, SIGNED, true, false>(maps, p, smem, stream);
+    return fb8 ? launch<MT, SIGNED, false, true>(maps, p, smem, stream)
+               : launch<MT, SIGNED, false, false>(maps, p, smem, stream);
+}
+
+int dispatch(bool is_signed, bool zp, bool fb8, int MT, const DecodeMaps& maps, const DecodeParams& p, size_t smem,
+             cudaStream_t stream) {
+    if (MT == 1) return is_signed ? dispatch_zp<1, true>(zp, fb8, maps, p, smem, stream)
+                                  : dispatch_zp<1, false>(zp, fb8, maps, p, smem, stream);
+    return is_signed ? dispatch_zp<2, true>(zp, fb8, maps, p, smem, stream)
+                     : dispatch_zp<2, false>(zp, fb8, maps, p, smem, stream);
+}
+
+// Shared memory an SM offers two co-resident CTAs, and one CTA alone.
+void smem_budget(size_t* two, size_t* one) {
+    static size_t b2 = 0, b1 = 0;
+    if (!b1) {
+        int dev = 0, per_sm = 0, optin = 0, reserved = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+        b2 = (size_t)(per_sm / 2 - reserved);
+        b1 = (size_t)optin;
+    }
+    *two = b2;
+    *one = b1;
+}
+
+}  // namespace
+
+int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
+                   int K, int group, cudaStream_t stream) {
+    const int KW = K / 8;
+    const int gw = group / 8;
+    if (M > 16 || (long long)M * K > 32768) return T4B_ERR_UNSUPPORTED;
+    if ((K % 128) != 0 || (N % 8) != 0) return T4B_ERR_UNSUPPORTED;
+    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(S, 16) || (Z && !aligned(Z, 16))) return T4B_ERR_UNSUPPORTED;
+    const int MT = (M <= 8) ? 1 : 2;
+    const int warps = (MT == 1) ? Shape<1>::kWarps : Shape<2>::kWarps;
+    const int rows_narrow = 16 * warps, rows_wide = 8 * warps;
+    // a flush block (8 or 16 word rows) and a scale box (rows_wide rows) must
+    // each lie in one group
+    auto box_rows = [&](int rows) { return rows % gw == 0 ? rows / gw : (gw % rows == 0 ? 1 : 0); };
+    if (!(gw == 8 || gw >= 16) || !box_rows(rows_wide) || !box_rows(rows_narrow)) return T4B_ERR_UNSUPPORTED;
+    DecodeParams p;
+    p.A = static_cast<const uint16_t*>(A);
+    p.C = static_cast<uint16_t*>(C);
+    p.M = M; p.N = N; p.K = K; p.KW = KW;
+    p.KWp = (KW + rows_narrow - 1) / rows_narrow * rows_narrow;
+    p.T = (N + kBoxCols - 1) / kBoxCols;
+    p.G = p.T < sm_count() ? p.T : sm_count();
+    if ((long long)p.T * p.G >= (1ll << 32)) return T4B_ERR_UNSUPPORTED;
+    p.gw = gw;
+    p.gw_shift = -1;
+    if ((gw & (gw - 1)) == 0) {
+        int sh = 0;
+        while ((1 << sh) < gw) ++sh;
+        p.gw_shift = sh;
+    }
+    p.fb = (gw == 8) ? 8 : 16;
+    p.sbr_wide = box_rows(rows_wide);
+    p.sbr_narrow = box_rows(rows_narrow);
+    p.s_bytes = std::max(p.sbr_wide * 128, p.sbr_narrow * 64);
+    p.s_wide = (KW + rows_wide - 1) / rows_wide;
+    p.s_narrow = (KW + rows_narrow - 1) / rows_narrow;
+    p.act_bytes = M * (p.KWp + 2) * 16;
+    p.sum_floats = (p.KWp / p.fb) * 8 * MT;
+    p.red_floats = warps * 32 * M;
+    p.kwdiv = make_fastdiv((uint32_t)p.KWp);
+    const int weight_bytes = warps * 2048;
+    p.slot_bytes = (weight_bytes + p.s_bytes * (Z ? 2 : 1) + 1023) / 1024 * 1024;
+    const size_t fixed = 1024 + (size_t)p.act_bytes + 4 * (size_t)(p.sum_floats + p.red_floats) + kMaxStages * 12 + 16;
+    // two CTAs per SM (one computing, one prefetching the next kernel's
+    // stages) when the ring still gets 2+ stages; else one CTA, deeper ring
+    size_t two = 0, one = 0;
+    smem_budget(&two, &one);
+    int stages = fixed < two ? (int)((two - fixed) / p.slot_bytes) : 0;
+    if (stages > 8) stages = 8;
+    if (stages < 2) {
+        stages = fixed < one ? (int)((one - fixed) / p.slot_bytes) : 0;
+        if (stages > kMaxStages) stages = kMaxStages;
+    }
+    if (stages < 2) return T4B_ERR_UNSUPPORTED;
+    p.stages = stages;
+    // A CTA whose weights fit in the ring fetches all of them before the
+    // previous kernel ends.  One that must stream more than a ring's worth
+    // fetches a single stage early: a deep early prefetch from every SM would
+    // queue ahead of the previous kernel's own loads (its refills and its
+    // activations) and delay the very kernel it waits for.
+    const long long cta_bytes = (long long)((p.T + p.G - 1) / p.G) * kBoxCols * KW * 4;
+    p.early = (cta_bytes <= (long long)stages * weight_bytes) ? stages : 1;
+    const size_t smem = fixed + (size_t)stages * p.slot_bytes;
+
+    DecodeMaps maps;
+    if (!make_tmap_2d_ex(&maps.w_wide, false, W, (uint64_t)KW, (uint64_t)N, rows_wide, kBoxCols, 64, 128) ||
+        !make_tmap_2d_ex(&maps.w_narrow, false, W, (uint64_t)KW, (uint64_t)N, rows_narrow, kBoxCols, 64, 128) ||
+        !make_tmap_2d_ex(&maps.s_wide, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_wide, 4 * kBoxCols, 0, 0) ||
+        !make_tmap_2d_ex(&maps.s_narrow, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_narrow, 2 * kBoxCols, 0, 0))
+        return T4B_ERR_UNSUPPORTED;
+    if (Z) {
+        if (!make_tmap_2d_ex(&maps.z_wide, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_wide, 4 * kBoxCols, 0, 0) ||
+            !make_tmap_2d_ex(&maps.z_narrow, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_narrow, 2 * kBoxCols, 0, 0))
+            return T4B_ERR_UNSUPPORTED;
+    } else {
+        maps.z_wide = maps.s_wide;       // never read
+        maps.z_narrow = maps.s_narrow;
+    }
+    Workspace ws;
+    const int st = acquire_workspace(stream, 0, 0, &ws);
+    if (st != T4B_OK) return st;
+    p.err = ws.error;
+    return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, maps, p, smem, stream);
+}
+
+}  // namespace t4b

@@ -22,6 +22,12 @@ bool make_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 bool make_tmap_f16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
                       uint32_t box_cols);
 
+// General form: element type u32 or fp16, swizzle 0 / 32 / 64 / 128 bytes
+// (a box row may not be wider than the swizzle span), L2 promotion
+// 0 / 64 / 128 / 256 bytes.
+bool make_tmap_2d_ex(CUtensorMap* map, bool fp16, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                     uint32_t box_cols, int swizzle_bytes, int l2_promotion_bytes);
+
 // --------------------------------------------------------------- device side
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -72,10 +72,17 @@ SHAPES = [
     (9, 96, 64, 32, None),           # two m-tiles
     (17, 256, 192, 128, "int"),      # M > 16: row chunks
     (33, 128, 64, None, None),
+    (2, 1024, 200, None, "frac"),    # per-column scales, N tail inside a 16-column tile
+    (3, 512, 520, 256, "int"),       # odd tile count, group of 32 word rows
+    (2, 512, 14336, 64, "int"),      # 6-7 tiles per CTA (4 + 2/3 tile groups), 8-row flush blocks
+    (12, 2048, 2720, 128, "frac"),   # M > 8: two batch tiles
+    (1, 1024, 9600, 128, None),      # 4-5 tiles per CTA (a lone last tile)
+    (3, 256, 7904, 128, "int"),      # 3-4 tiles per CTA (three-tile groups)
+    (4, 1024, 512, 32, None),        # group 32: not the decode kernel's (falls back)
 ]
 
 
-@pytest.fixture(params=["auto", "generic"])
+@pytest.fixture(params=["auto", "stream", "generic"])
 def gemv_kernel(request, cuda_device):
     prev = t4_cuda_b200.set_gemv_kernel(request.param)
     yield request.param

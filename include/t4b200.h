@@ -51,11 +51,12 @@ int t4b_last_cuda_error(void);
 /* Library ABI version: (major << 16) | minor. */
 int t4b_version(void);
 
-/* Reads (and, if `clear`, resets) the device error word of the workspace this
- * library keeps for `stream` on the current device: bit 0 = a kernel gave up a
- * bounded wait (its output is then invalid).  Synchronizes `stream`; do not
- * call while the stream is being captured.  No library extension: this has no
- * counterpart in the reference, which has no device-side error reporting. */
+/* Reads (and, if `clear`, resets) the library's device error words on the
+ * current device -- the decode GEMV's (one per device) ORed with the one in the
+ * workspace kept for `stream` (if any): bit 0 = a kernel gave up a bounded wait
+ * (its output is then invalid).  Synchronizes `stream`; do not call while the
+ * stream is being captured.  No counterpart in the reference, which has no
+ * device-side error reporting. */
 int t4b_device_error(void* stream, unsigned* out, int clear);
 
 /* Kernel selection for the W4A16 matmul (argument of t4b_set_gemv_kernel). */

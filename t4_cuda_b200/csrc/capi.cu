@@ -171,21 +171,30 @@ int t4b_version(void) { return (1 << 16) | 1; }
 int t4b_device_error(void* stream, unsigned* out, int clear) {
     if (!out) return T4B_ERR_NULL_POINTER;
     *out = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // the decode GEMV keeps one word per device
+    unsigned decode = 0;
+    int st = t4b::decode_device_error(s, &decode, clear != 0);
+    if (st != T4B_OK) return st;
+    *out = decode;
+    // the split-tile GEMV keeps one in the workspace of each stream
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return t4b::record_cuda_error(e);
     void* base = nullptr;
     {
         std::lock_guard<std::mutex> lock(t4b::g_ws_mutex);
-        auto it = t4b::g_ws.find({dev, static_cast<cudaStream_t>(stream)});
+        auto it = t4b::g_ws.find({dev, s});
         if (it == t4b::g_ws.end()) return T4B_OK;
         base = it->second.base;
     }
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    e = cudaMemcpyAsync(out, base, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+    unsigned word = 0;
+    e = cudaMemcpyAsync(&word, base, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess && clear) e = cudaMemsetAsync(base, 0, sizeof(unsigned), s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    return e == cudaSuccess ? T4B_OK : t4b::record_cuda_error(e);
+    if (e != cudaSuccess) return t4b::record_cuda_error(e);
+    *out |= word;
+    return T4B_OK;
 }
 
 }  // extern "C"

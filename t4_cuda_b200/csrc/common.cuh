@@ -35,6 +35,10 @@ int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, 
 int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
                    int K, int group, cudaStream_t stream);
 
+// Reads (and optionally clears) the decode GEMV's device error word on the
+// current device; synchronizes `stream`.
+int decode_device_error(cudaStream_t stream, unsigned* out, bool clear);
+
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Division by a runtime constant d >= 1 for numerators n < 2^31:

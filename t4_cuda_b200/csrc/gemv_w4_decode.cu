@@ -46,7 +46,6 @@
 
 #include "common.cuh"
 #include "tma.cuh"
-#include "workspace.h"
 
 namespace t4b {
 namespace {
@@ -65,10 +64,14 @@ struct Shape {
     static constexpr int kRowsWide = 8 * kWarps;               // stage rows, 2 warp columns (3-4 tiles)
 };
 
+// Device error word of this kernel (bit 0: a bounded wait gave up), one per
+// device.  Device code sets it by name, so a call needs no workspace and can
+// be captured into a CUDA graph on any stream; decode_device_error() reads it.
+__device__ unsigned g_decode_error = 0;
+
 struct DecodeParams {
     const uint16_t* A;
     uint16_t* C;
-    unsigned* err;
     int M, N, K, KW;
     int KWp;            // word rows padded to a multiple of the narrow stage (resident activations)
     int T, G;           // 16-column tiles, CTAs
@@ -390,7 +393,7 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
             if (!aborted && !mbar_wait_bounded(&full[slot], phase, kWaitLimitNs)) {
                 aborted = true;
                 sflag[0] = 1;
-                atomicOr(p.err, kErrTimeout);
+                atomicOr(&g_decode_error, kErrTimeout);
             }
             if (!aborted) {
                 const uint32_t st = ring_a + (uint32_t)slot * p.slot_bytes;
@@ -555,6 +558,15 @@ void smem_budget(size_t* two, size_t* one) {
 
 }  // namespace
 
+int decode_device_error(cudaStream_t stream, unsigned* out, bool clear) {
+    unsigned* word = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&word), g_decode_error);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, word, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(word, 0, sizeof(unsigned), stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e == cudaSuccess ? T4B_OK : record_cuda_error(e);
+}
+
 int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
                    int K, int group, cudaStream_t stream) {
     const int KW = K / 8;
@@ -615,7 +627,7 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
     // queue ahead of the previous kernel's own loads (its refills and its
     // activations) and delay the very kernel it waits for.
     const long long cta_bytes = (long long)((p.T + p.G - 1) / p.G) * kBoxCols * KW * 4;
-    p.early = (cta_bytes <= (long long)stages * weight_bytes) ? stages : 1;
+    p.early = (cta_bytes <= (long long)stages * weight_bytes) ? stages : (stages > 2 ? 2 : 1);
     const size_t smem = fixed + (size_t)stages * p.slot_bytes;
 
     DecodeMaps maps;
@@ -632,10 +644,6 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
         maps.z_wide = maps.s_wide;       // never read
         maps.z_narrow = maps.s_narrow;
     }
-    Workspace ws;
-    const int st = acquire_workspace(stream, 0, 0, &ws);
-    if (st != T4B_OK) return st;
-    p.err = ws.error;
     return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, maps, p, smem, stream);
 }
 

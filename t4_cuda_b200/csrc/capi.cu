@@ -177,6 +177,11 @@ int t4b_device_error(void* stream, unsigned* out, int clear) {
     int st = t4b::decode_device_error(s, &decode, clear != 0);
     if (st != T4B_OK) return st;
     *out = decode;
+    // so does the prefill GEMM
+    unsigned gemm = 0;
+    st = t4b::gemm_tc_device_error(s, &gemm, clear != 0);
+    if (st != T4B_OK) return st;
+    *out |= gemm;
     // the split-tile GEMV keeps one in the workspace of each stream
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

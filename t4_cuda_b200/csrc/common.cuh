@@ -39,6 +39,12 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
 // current device; synchronizes `stream`.
 int decode_device_error(cudaStream_t stream, unsigned* out, bool clear);
 
+// Prefill GEMM on tcgen05 / TMEM (M > 16, K % 64 == 0, group % 64 == 0);
+// T4B_ERR_UNSUPPORTED (without launching) for shapes it does not take.
+int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N, int K,
+               int group, cudaStream_t stream);
+int gemm_tc_device_error(cudaStream_t stream, unsigned* out, bool clear);
+
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Division by a runtime constant d >= 1 for numerators n < 2^31:

@@ -1,0 +1,352 @@
+// Prefill W4A16 GEMM on the 5th-generation tensor cores (tcgen05, TMEM):
+//
+//   C[M, N] = A[M, K] x dequant(W)[K, N],  W int32 [K/8, N], group scales [K/g, N]
+//
+// for M > 16, K % 64 == 0 and g % 64 == 0.
+//
+// One CTA computes a 128 x 256 tile of C with a single-CTA tcgen05.mma
+// (M = 128, N = 256, K = 16 per instruction, fp16 in, fp32 accumulate in
+// TMEM, 256 TMEM columns), looping over K in steps of 64 through a 3-stage
+// shared-memory ring.  Warp roles:
+//   warp 0      one thread issues the TMA copies of a stage: the 128 x 64 tile
+//               of A (128-byte swizzle, the UMMA K-major canonical layout), the
+//               8 x 256 tile of packed words, one row of scales (and zero
+//               points) -- each K step lies inside one scale group;
+//   warp 1      allocates TMEM; one thread issues the MMAs of a stage once A
+//               and the dequantized B are in place and commits them to the
+//               stage's "empty" barrier, which frees the slot;
+//   warps 2-5   dequantize the packed tile into B (256 x 64 fp16, K-major,
+//               128-byte swizzle) -- the weight rounded exactly as the contract
+//               says, fp16(q * s) (fp16(fp32((q - z) * s)) with zero points) --
+//               and, after the last K step, drain the accumulator from TMEM,
+//               convert it to fp16 and store C.
+// Every wait on an mbarrier is bounded; a timeout sets this file's device
+// error word, stops the pipeline and still frees TMEM before the CTA exits.
+#include "common.cuh"
+#include "tma.cuh"
+
+namespace t4b {
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kStages = 3;
+constexpr int kThreads = 192;                       // 6 warps
+constexpr int kABytes = kBM * kBK * 2;              // 16 KB
+constexpr int kWBytes = (kBK / 8) * kBN * 4;        // 8 KB packed
+constexpr int kSBytes = kBN * 2;                    // one row of scales
+constexpr int kBBytes = kBN * kBK * 2;              // 32 KB dequantized
+constexpr int kStageBytes = kABytes + kBBytes + kWBytes + 2 * kSBytes;   // A, B, packed, scales, zero points
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr unsigned kErrTimeout = 1u;
+
+// Device error word of this kernel, one per device (see gemm_tc_device_error).
+__device__ unsigned g_gemm_tc_error = 0;
+
+struct GemmParams {
+    uint16_t* C;
+    int M, N, K;
+    int gw_steps;       // K steps (of 64) per scale group (0: a single group, per-column scales)
+    int ksteps;
+};
+
+struct GemmMaps {
+    CUtensorMap a;      // A [M, K] fp16, box 64 x 128, 128-byte swizzle
+    CUtensorMap w;      // W [K/8, N] u32, box 256 x 8
+    CUtensorMap s;      // scales [K/g, N] fp16, box 256 x 1
+    CUtensorMap z;      // zero points, same (unused without them)
+};
+
+// ---- tcgen05 wrappers (PTX ISA 8.7, sm_100a)
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    // K-major, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes
+    // apart (stride byte offset), leading byte offset unused (1), version 1.
+    uint64_t d = (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;                 // leading byte offset (16 B units)
+    d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset
+    d |= (uint64_t)1 << 46;                 // descriptor version
+    d |= (uint64_t)2 << 61;                 // layout: 128-byte swizzle
+    return d;
+}
+
+// kind::f16 instruction descriptor: fp16 A and B (K-major), fp32 accumulator.
+constexpr uint32_t kInstrDesc = (1u << 4)                       // D format fp32
+                              | ((uint32_t)(kBN >> 3) << 17)    // N
+                              | ((uint32_t)(kBM >> 4) << 24);   // M
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :
+        : "r"(tmem_d), "l"(da), "l"(db), "r"(kInstrDesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Bounded wait; on timeout records the error and raises the CTA's abort flag.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (*abort_flag) return false;
+    if (mbar_wait_bounded(bar, parity, kWaitLimitNs)) return true;
+    *abort_flag = 1;
+    atomicOr(&g_gemm_tc_error, kErrTimeout);
+    return false;
+}
+
+// Eight consecutive K values (one packed word) of one column as four fp16x2
+// in natural order, each the exact integer q (signed or unsigned nibble).
+template <bool SIGNED>
+__device__ __forceinline__ void unpack_natural(uint32_t w, uint32_t (&q)[4]) {
+    // byte i of w holds (q_{2i}, q_{2i+1}) in its low / high nibble; copy it to
+    // bytes 0 and 2, then take the low nibble under exponent 2^10 (1024 + n)
+    // and the high nibble of byte 2 under exponent 2^6 (64 + n).
+    constexpr uint32_t kMask = 0x00F0000Fu;
+    constexpr uint32_t kMagic = SIGNED ? 0x54806408u : 0x54006400u;   // signed: top bit of each nibble flipped
+    constexpr uint32_t kBias = SIGNED ? 0x54806408u : 0x54006400u;    // 72 / 1032 or 64 / 1024
+    constexpr int kLut = SIGNED ? 0x6A : 0xEA;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t x = prmt(w, w, 0x4040u + 0x1111u * (uint32_t)i);   // bytes (i, i, i, i)
+        q[i] = h2_sub(lop3<kLut>(x, kMask, kMagic), kBias);
+    }
+}
+
+template <bool SIGNED, bool HAS_ZP>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    // stage s: [A 16 KB][B 32 KB][packed 8 KB][scales 512][zero points 512]
+    uint64_t* full_tma = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
+    uint64_t* full_b = full_tma + kStages;
+    uint64_t* empty = full_b + kStages;
+    uint64_t* acc_full = empty + kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full_tma[s], 1);
+            mbar_init(&full_b[s], 4);      // one arrival per dequant warp
+            mbar_init(&empty[s], 1);       // tcgen05.commit
+        }
+        mbar_init(acc_full, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&maps.a);
+        prefetch_tmap(&maps.w);
+        prefetch_tmap(&maps.s);
+        if constexpr (HAS_ZP) prefetch_tmap(&maps.z);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kBN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            for (int i = 0; i < p.ksteps; ++i) {
+                const int s = i % kStages;
+                const uint32_t ph = (uint32_t)((i / kStages) & 1);
+                if (i >= kStages && !wait_or_abort(&empty[s], ph ^ 1u, abort_flag)) break;
+                uint8_t* st = base + s * kStageBytes;
+                const int srow = p.gw_steps ? i / p.gw_steps : 0;
+                mbar_arrive_expect_tx(&full_tma[s], kABytes + kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
+                tma_load_2d(st, &maps.a, i * kBK, m0, &full_tma[s]);
+                tma_load_2d(st + kABytes + kBBytes, &maps.w, n0, i * (kBK / 8), &full_tma[s]);
+                tma_load_2d(st + kABytes + kBBytes + kWBytes, &maps.s, n0, srow, &full_tma[s]);
+                if constexpr (HAS_ZP)
+                    tma_load_2d(st + kABytes + kBBytes + kWBytes + kSBytes, &maps.z, n0, srow, &full_tma[s]);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            bool ok = true;
+            for (int i = 0; i < p.ksteps && ok; ++i) {
+                const int s = i % kStages;
+                const uint32_t ph = (uint32_t)((i / kStages) & 1);
+                ok = wait_or_abort(&full_tma[s], ph, abort_flag) && wait_or_abort(&full_b[s], ph, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(base + s * kStageBytes);
+                const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                    tc_mma(tmem_d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
+                           (i > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(&empty[s]);
+            }
+            tc_commit(acc_full);     // fires once every MMA issued above has completed
+        }
+    } else {
+        // ---------------- dequant warpgroup (warps 2..5), then epilogue
+        const int t = threadIdx.x - 64;             // 0..127: columns t and t + 128
+        for (int i = 0; i < p.ksteps; ++i) {
+            const int s = i % kStages;
+            const uint32_t ph = (uint32_t)((i / kStages) & 1);
+            // B[s] is free: the producer reused this slot only after its MMAs completed
+            if (!wait_or_abort(&full_tma[s], ph, abort_flag)) break;
+            uint8_t* st = base + s * kStageBytes;
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + kABytes + kBBytes);
+            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kABytes + kBBytes + kWBytes);
+            uint8_t* bt = st + kABytes;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int n = t + 128 * h;
+                const uint16_t sbits = sp[n];
+                const uint32_t s2 = h2_dup(sbits);
+                float zf = 0.f, sf = 0.f;
+                if constexpr (HAS_ZP) {
+                    zf = h_to_f(sp[kBN + n]);
+                    sf = h_to_f(sbits);
+                }
+#pragma unroll
+                for (int j = 0; j < kBK / 8; ++j) {
+                    const uint32_t w = wp[j * kBN + n];
+                    uint32_t q[4];
+                    unpack_natural<SIGNED>(w, q);
+                    uint4 o;
+                    uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if constexpr (HAS_ZP) {
+                            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[k]));
+                            ov[k] = f2_to_h2((f.x - zf) * sf, (f.y - zf) * sf);
+                        } else {
+                            ov[k] = h2_mul(q[k], s2);
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(bt + n * 128 + ((j ^ (n & 7)) << 4)) = o;
+                }
+            }
+            fence_proxy_async_smem();      // generic-proxy writes of B before the MMA reads them
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_b[s]);
+        }
+        // ---------------- epilogue: TMEM lanes 32 * (warp % 4) .. +31 = rows of the tile
+        const bool ok = wait_or_abort(acc_full, 0, abort_flag);
+        tc_fence_after();
+        const int quarter = warp & 3;
+        const int row = m0 + 32 * quarter + lane;
+        if (ok) {
+            for (int c0 = 0; c0 < kBN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+                if (row < p.M) {
+                    uint16_t* crow = p.C + (size_t)row * p.N + n0 + c0;
+                    if (n0 + c0 + 32 <= p.N && (p.N % 8) == 0) {
+#pragma unroll
+                        for (int k = 0; k < 32; k += 8) {
+                            uint4 o;
+                            o.x = f2_to_h2(__uint_as_float(v[k + 0]), __uint_as_float(v[k + 1]));
+                            o.y = f2_to_h2(__uint_as_float(v[k + 2]), __uint_as_float(v[k + 3]));
+                            o.z = f2_to_h2(__uint_as_float(v[k + 4]), __uint_as_float(v[k + 5]));
+                            o.w = f2_to_h2(__uint_as_float(v[k + 6]), __uint_as_float(v[k + 7]));
+                            *reinterpret_cast<uint4*>(crow + k) = o;
+                        }
+                    } else {
+                        for (int k = 0; k < 32; ++k)
+                            if (n0 + c0 + k < p.N) crow[k] = __half_as_ushort(__float2half_rn(__uint_as_float(v[k])));
+                    }
+                }
+            }
+        }
+    }
+
+    // ---------------- teardown: no MMA may still be writing TMEM when it is freed
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag && threadIdx.x == 32) {
+        // the issuer committed acc_full after its last MMA; wait for it (bounded)
+        mbar_wait_bounded(acc_full, 0, kWaitLimitNs / 4);
+        // and for copies still landing in the ring
+        for (int s = 0; s < kStages; ++s) mbar_wait_bounded(&full_tma[s], 0, kWaitLimitNs / 8);
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kBN));
+    }
+}
+
+template <bool SIGNED, bool HAS_ZP>
+int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
+    auto kern = gemm_w4_tc_kernel<SIGNED, HAS_ZP>;
+    const size_t smem = 1024 + (size_t)kStages * kStageBytes + (3 * kStages + 1) * 8 + 16;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        configured = true;
+    }
+    dim3 grid((p.N + kBN - 1) / kBN, (p.M + kBM - 1) / kBM, 1);
+    kern<<<grid, kThreads, smem, stream>>>(maps, p);
+    return check_launch();
+}
+
+}  // namespace
+
+int gemm_tc_device_error(cudaStream_t stream, unsigned* out, bool clear) {
+    unsigned* word = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&word), g_gemm_tc_error);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, word, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(word, 0, sizeof(unsigned), stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e == cudaSuccess ? T4B_OK : record_cuda_error(e);
+}
+
+int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N, int K,
+               int group, cudaStream_t stream) {
+    if (M <= 16 || (K % kBK) != 0 || (group % kBK) != 0 || (N % 8) != 0) return T4B_ERR_UNSUPPORTED;
+    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(S, 16) || (Z && !aligned(Z, 16)) || !aligned(C, 16))
+        return T4B_ERR_UNSUPPORTED;
+    GemmParams p;
+    p.C = static_cast<uint16_t*>(C);
+    p.M = M; p.N = N; p.K = K;
+    p.ksteps = K / kBK;
+    p.gw_steps = (group >= K) ? 0 : group / kBK;
+    GemmMaps maps;
+    if (!make_tmap_2d_ex(&maps.a, true, A, (uint64_t)M, (uint64_t)K, kBM, kBK, 128, 256) ||
+        !make_tmap_2d_ex(&maps.w, false, W, (uint64_t)(K / 8), (uint64_t)N, kBK / 8, kBN, 0, 256) ||
+        !make_tmap_2d_ex(&maps.s, true, S, (uint64_t)(K / group), (uint64_t)N, 1, kBN, 0, 0))
+        return T4B_ERR_UNSUPPORTED;
+    if (Z) {
+        if (!make_tmap_2d_ex(&maps.z, true, Z, (uint64_t)(K / group), (uint64_t)N, 1, kBN, 0, 0))
+            return T4B_ERR_UNSUPPORTED;
+    } else {
+        maps.z = maps.s;
+    }
+    if (is_signed) return Z ? launch<true, true>(maps, p, stream) : launch<true, false>(maps, p, stream);
+    return Z ? launch<false, true>(maps, p, stream) : launch<false, false>(maps, p, stream);
+}
+
+}  // namespace t4b

@@ -283,6 +283,10 @@ int fused_gemm(const void* A, const void* W, const void* S, const void* Z, void*
     if (!aligned(A, 16) || !aligned(W, 4) || !aligned(S, 2) || !aligned(C, 2) || (Z && !aligned(Z, 2)))
         return T4B_ERR_MISALIGNED;
     const int choice = g_gemv_kernel.load();
+    if (choice == T4B_GEMV_AUTO && M > kStreamMaxM) {
+        const int st = gemm_w4_tc(SIGNED, A, W, S, Z, C, M, N, K, group, static_cast<cudaStream_t>(stream_));
+        if (st != T4B_ERR_UNSUPPORTED) return st;
+    }
     if (choice == T4B_GEMV_AUTO && M <= kStreamMaxM) {
         const int st = gemv_w4_decode(SIGNED, A, W, S, Z, C, M, N, K, group, static_cast<cudaStream_t>(stream_));
         if (st != T4B_ERR_UNSUPPORTED) return st;

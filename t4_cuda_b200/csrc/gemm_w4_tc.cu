@@ -15,11 +15,12 @@
 //   warp 1      allocates TMEM; one thread issues the MMAs of a stage once A
 //               and the dequantized B are in place and commits them to the
 //               stage's "empty" barrier, which frees the slot;
-//   warps 2-5   dequantize the packed tile into B (256 x 64 fp16, K-major,
-//               128-byte swizzle) -- the weight rounded exactly as the contract
-//               says, fp16(q * s) (fp16(fp32((q - z) * s)) with zero points) --
-//               and, after the last K step, drain the accumulator from TMEM,
-//               convert it to fp16 and store C.
+//   warps 2-9   two warpgroups dequantize the packed tile into B (256 x 64
+//               fp16, K-major, 128-byte swizzle; one column per thread) -- the
+//               weight rounded exactly as the contract says, fp16(q * s)
+//               (fp16(fp32((q - z) * s)) with zero points) -- and, after the
+//               last K step, drain the accumulator from TMEM (each warpgroup
+//               128 of the 256 columns), convert it to fp16 and store C.
 // Every wait on an mbarrier is bounded; a timeout sets this file's device
 // error word, stops the pipeline and still frees TMEM before the CTA exits.
 #include "common.cuh"
@@ -30,7 +31,8 @@ namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
 constexpr int kStages = 3;
-constexpr int kThreads = 192;                       // 6 warps
+constexpr int kDqWarps = 8;                         // dequant / epilogue warps (two warpgroups)
+constexpr int kThreads = 64 + 32 * kDqWarps;         // + TMA warp + MMA warp
 constexpr int kABytes = kBM * kBK * 2;              // 16 KB
 constexpr int kWBytes = (kBK / 8) * kBN * 4;        // 8 KB packed
 constexpr int kSBytes = kBN * 2;                    // one row of scales
@@ -149,7 +151,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full_tma[s], 1);
-            mbar_init(&full_b[s], 4);      // one arrival per dequant warp
+            mbar_init(&full_b[s], kDqWarps);   // one arrival per dequant warp
             mbar_init(&empty[s], 1);       // tcgen05.commit
         }
         mbar_init(acc_full, 1);
@@ -208,8 +210,8 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
             tc_commit(acc_full);     // fires once every MMA issued above has completed
         }
     } else {
-        // ---------------- dequant warpgroup (warps 2..5), then epilogue
-        const int t = threadIdx.x - 64;             // 0..127: columns t and t + 128
+        // ---------------- dequant warpgroups (warps 2..9), then epilogue
+        const int t = threadIdx.x - 64;             // 0..255: column t
         for (int i = 0; i < p.ksteps; ++i) {
             const int s = i % kStages;
             const uint32_t ph = (uint32_t)((i / kStages) & 1);
@@ -219,9 +221,8 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
             const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + kABytes + kBBytes);
             const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kABytes + kBBytes + kWBytes);
             uint8_t* bt = st + kABytes;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int n = t + 128 * h;
+            {
+                const int n = t;
                 const uint16_t sbits = sp[n];
                 const uint32_t s2 = h2_dup(sbits);
                 float zf = 0.f, sf = 0.f;
@@ -255,10 +256,11 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         // ---------------- epilogue: TMEM lanes 32 * (warp % 4) .. +31 = rows of the tile
         const bool ok = wait_or_abort(acc_full, 0, abort_flag);
         tc_fence_after();
-        const int quarter = warp & 3;
+        const int quarter = warp & 3;                       // TMEM lanes this warp may read
+        const int half = (warp - 2) >> 2;                   // which 128 columns
         const int row = m0 + 32 * quarter + lane;
         if (ok) {
-            for (int c0 = 0; c0 < kBN; c0 += 32) {
+            for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
                 if (row < p.M) {

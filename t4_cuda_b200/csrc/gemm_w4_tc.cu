@@ -6,21 +6,25 @@
 //
 // One CTA computes a 128 x 256 tile of C with a single-CTA tcgen05.mma
 // (M = 128, N = 256, K = 16 per instruction, fp16 in, fp32 accumulate in
-// TMEM, 256 TMEM columns), looping over K in steps of 64 through a 3-stage
-// shared-memory ring.  Warp roles:
+// TMEM, 256 TMEM columns), looping over K in steps of 64.  Two shared-memory
+// rings: a 5-deep one of TMA copies (A, packed words, scales), deep enough to
+// cover the copy latency, and a 2-deep one of dequantized B tiles between the
+// dequant warps and the MMA.  Warp roles:
 //   warp 0      one thread issues the TMA copies of a stage: the 128 x 64 tile
 //               of A (128-byte swizzle, the UMMA K-major canonical layout), the
 //               8 x 256 tile of packed words, one row of scales (and zero
 //               points) -- each K step lies inside one scale group;
 //   warp 1      allocates TMEM; one thread issues the MMAs of a stage once A
 //               and the dequantized B are in place and commits them to the
-//               stage's "empty" barrier, which frees the slot;
-//   warps 2-9   two warpgroups dequantize the packed tile into B (256 x 64
-//               fp16, K-major, 128-byte swizzle; one column per thread) -- the
-//               weight rounded exactly as the contract says, fp16(q * s)
-//               (fp16(fp32((q - z) * s)) with zero points) -- and, after the
-//               last K step, drain the accumulator from TMEM (each warpgroup
-//               128 of the 256 columns), convert it to fp16 and store C.
+//               "empty" barriers of both slots it read, which frees them;
+//   warps 2-17  four warpgroups dequantize the packed tile into B (256 x 64
+//               fp16, K-major, 128-byte swizzle; a thread does one column and
+//               half the K step) -- the weight rounded exactly as the contract
+//               says, fp16(q * s) (fp16(fp32((q - z) * s)) with zero points) --
+//               and, after the last K step, drain the accumulator from TMEM
+//               (each warpgroup 64 of the 256 columns), convert it to fp16 and
+//               store C.  Sixteen warps, because a warpgroup's dequant is
+//               latency-bound: with fewer the tensor pipe idles waiting for B.
 // Every wait on an mbarrier is bounded; a timeout sets this file's device
 // error word, stops the pipeline and still frees TMEM before the CTA exits.
 #include "common.cuh"
@@ -30,14 +34,17 @@ namespace t4b {
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 3;
-constexpr int kDqWarps = 8;                         // dequant / epilogue warps (two warpgroups)
+constexpr int kTmaStages = 5;
+constexpr int kBStages = 2;
+constexpr int kDqWarps = 16;                        // dequant / epilogue warps (four warpgroups)
 constexpr int kThreads = 64 + 32 * kDqWarps;         // + TMA warp + MMA warp
 constexpr int kABytes = kBM * kBK * 2;              // 16 KB
 constexpr int kWBytes = (kBK / 8) * kBN * 4;        // 8 KB packed
 constexpr int kSBytes = kBN * 2;                    // one row of scales
 constexpr int kBBytes = kBN * kBK * 2;              // 32 KB dequantized
-constexpr int kStageBytes = kABytes + kBBytes + kWBytes + 2 * kSBytes;   // A, B, packed, scales, zero points
+constexpr int kTmaStageBytes = kABytes + kWBytes + 2 * kSBytes;   // A, packed, scales, zero points (25 KB)
+constexpr int kRingBytes = kTmaStages * kTmaStageBytes + kBStages * kBBytes;
+constexpr int kBarriers = 2 * kTmaStages + 2 * kBStages + 1;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr unsigned kErrTimeout = 1u;
 
@@ -137,11 +144,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    // stage s: [A 16 KB][B 32 KB][packed 8 KB][scales 512][zero points 512]
-    uint64_t* full_tma = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
-    uint64_t* full_b = full_tma + kStages;
-    uint64_t* empty = full_b + kStages;
-    uint64_t* acc_full = empty + kStages;
+    // TMA slot s: [A 16 KB][packed 8 KB][scales 512][zero points 512]; then the B slots (32 KB each)
+    uint8_t* bring = base + kTmaStages * kTmaStageBytes;
+    uint64_t* full_tma = reinterpret_cast<uint64_t*>(base + kRingBytes);
+    uint64_t* empty_tma = full_tma + kTmaStages;
+    uint64_t* full_b = empty_tma + kTmaStages;
+    uint64_t* empty_b = full_b + kBStages;
+    uint64_t* acc_full = empty_b + kBStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -149,10 +158,13 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kTmaStages; ++s) {
             mbar_init(&full_tma[s], 1);
-            mbar_init(&full_b[s], kDqWarps);   // one arrival per dequant warp
-            mbar_init(&empty[s], 1);       // tcgen05.commit
+            mbar_init(&empty_tma[s], 1);          // tcgen05.commit
+        }
+        for (int s = 0; s < kBStages; ++s) {
+            mbar_init(&full_b[s], kDqWarps);      // one arrival per dequant warp
+            mbar_init(&empty_b[s], 1);            // tcgen05.commit
         }
         mbar_init(acc_full, 1);
         *abort_flag = 0;
@@ -176,96 +188,94 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         // ---------------- TMA producer
         if (lane == 0) {
             for (int i = 0; i < p.ksteps; ++i) {
-                const int s = i % kStages;
-                const uint32_t ph = (uint32_t)((i / kStages) & 1);
-                if (i >= kStages && !wait_or_abort(&empty[s], ph ^ 1u, abort_flag)) break;
-                uint8_t* st = base + s * kStageBytes;
+                const int s = i % kTmaStages;
+                const uint32_t ph = (uint32_t)((i / kTmaStages) & 1);
+                if (i >= kTmaStages && !wait_or_abort(&empty_tma[s], ph ^ 1u, abort_flag)) break;
+                uint8_t* st = base + s * kTmaStageBytes;
                 const int srow = p.gw_steps ? i / p.gw_steps : 0;
                 mbar_arrive_expect_tx(&full_tma[s], kABytes + kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
                 tma_load_2d(st, &maps.a, i * kBK, m0, &full_tma[s]);
-                tma_load_2d(st + kABytes + kBBytes, &maps.w, n0, i * (kBK / 8), &full_tma[s]);
-                tma_load_2d(st + kABytes + kBBytes + kWBytes, &maps.s, n0, srow, &full_tma[s]);
+                tma_load_2d(st + kABytes, &maps.w, n0, i * (kBK / 8), &full_tma[s]);
+                tma_load_2d(st + kABytes + kWBytes, &maps.s, n0, srow, &full_tma[s]);
                 if constexpr (HAS_ZP)
-                    tma_load_2d(st + kABytes + kBBytes + kWBytes + kSBytes, &maps.z, n0, srow, &full_tma[s]);
+                    tma_load_2d(st + kABytes + kWBytes + kSBytes, &maps.z, n0, srow, &full_tma[s]);
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
         if (lane == 0) {
-            bool ok = true;
-            for (int i = 0; i < p.ksteps && ok; ++i) {
-                const int s = i % kStages;
-                const uint32_t ph = (uint32_t)((i / kStages) & 1);
-                ok = wait_or_abort(&full_tma[s], ph, abort_flag) && wait_or_abort(&full_b[s], ph, abort_flag);
-                if (!ok) break;
+            for (int i = 0; i < p.ksteps; ++i) {
+                const int s = i % kTmaStages, b = i % kBStages;
+                if (!wait_or_abort(&full_tma[s], (uint32_t)((i / kTmaStages) & 1), abort_flag) ||
+                    !wait_or_abort(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag))
+                    break;
                 tc_fence_after();
-                const uint32_t a_addr = smem_addr(base + s * kStageBytes);
-                const uint32_t b_addr = a_addr + kABytes;
+                const uint32_t a_addr = smem_addr(base + s * kTmaStageBytes);
+                const uint32_t b_addr = smem_addr(bring + b * kBBytes);
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk)
                     tc_mma(tmem_d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
                            (i > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(&empty[s]);
+                tc_commit(&empty_tma[s]);     // both fire once these MMAs have read their operands
+                tc_commit(&empty_b[b]);
             }
             tc_commit(acc_full);     // fires once every MMA issued above has completed
         }
     } else {
-        // ---------------- dequant warpgroups (warps 2..9), then epilogue
-        const int t = threadIdx.x - 64;             // 0..255: column t
+        // ---------------- dequant warpgroups (warps 2..17), then epilogue
+        const int n = (threadIdx.x - 64) & (kBN - 1);       // column of the tile
+        const int j0 = ((threadIdx.x - 64) >> 8) * 4;       // word rows j0 .. j0 + 3 of the K step
         for (int i = 0; i < p.ksteps; ++i) {
-            const int s = i % kStages;
-            const uint32_t ph = (uint32_t)((i / kStages) & 1);
-            // B[s] is free: the producer reused this slot only after its MMAs completed
-            if (!wait_or_abort(&full_tma[s], ph, abort_flag)) break;
-            uint8_t* st = base + s * kStageBytes;
-            const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + kABytes + kBBytes);
-            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kABytes + kBBytes + kWBytes);
-            uint8_t* bt = st + kABytes;
-            {
-                const int n = t;
-                const uint16_t sbits = sp[n];
-                const uint32_t s2 = h2_dup(sbits);
-                float zf = 0.f, sf = 0.f;
-                if constexpr (HAS_ZP) {
-                    zf = h_to_f(sp[kBN + n]);
-                    sf = h_to_f(sbits);
-                }
+            const int s = i % kTmaStages, b = i % kBStages;
+            if (!wait_or_abort(&full_tma[s], (uint32_t)((i / kTmaStages) & 1), abort_flag)) break;
+            if (i >= kBStages && !wait_or_abort(&empty_b[b], (uint32_t)(((i / kBStages) & 1) ^ 1), abort_flag)) break;
+            const uint8_t* st = base + s * kTmaStageBytes;
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + kABytes);
+            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kABytes + kWBytes);
+            uint8_t* bt = bring + b * kBBytes;
+            const uint16_t sbits = sp[n];
+            const uint32_t s2 = h2_dup(sbits);
+            float zf = 0.f, sf = 0.f;
+            if constexpr (HAS_ZP) {
+                zf = h_to_f(sp[kBN + n]);
+                sf = h_to_f(sbits);
+            }
 #pragma unroll
-                for (int j = 0; j < kBK / 8; ++j) {
-                    const uint32_t w = wp[j * kBN + n];
-                    uint32_t q[4];
-                    unpack_natural<SIGNED>(w, q);
-                    uint4 o;
-                    uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = j0 + jj;
+                const uint32_t w = wp[j * kBN + n];
+                uint32_t q[4];
+                unpack_natural<SIGNED>(w, q);
+                uint4 o;
+                uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        if constexpr (HAS_ZP) {
-                            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[k]));
-                            ov[k] = f2_to_h2((f.x - zf) * sf, (f.y - zf) * sf);
-                        } else {
-                            ov[k] = h2_mul(q[k], s2);
-                        }
+                for (int k = 0; k < 4; ++k) {
+                    if constexpr (HAS_ZP) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[k]));
+                        ov[k] = f2_to_h2((f.x - zf) * sf, (f.y - zf) * sf);
+                    } else {
+                        ov[k] = h2_mul(q[k], s2);
                     }
-                    *reinterpret_cast<uint4*>(bt + n * 128 + ((j ^ (n & 7)) << 4)) = o;
                 }
+                *reinterpret_cast<uint4*>(bt + n * 128 + ((j ^ (n & 7)) << 4)) = o;
             }
             fence_proxy_async_smem();      // generic-proxy writes of B before the MMA reads them
             __syncwarp();
-            if (lane == 0) mbar_arrive(&full_b[s]);
+            if (lane == 0) mbar_arrive(&full_b[b]);
         }
         // ---------------- epilogue: TMEM lanes 32 * (warp % 4) .. +31 = rows of the tile
         const bool ok = wait_or_abort(acc_full, 0, abort_flag);
         tc_fence_after();
         const int quarter = warp & 3;                       // TMEM lanes this warp may read
-        const int half = (warp - 2) >> 2;                   // which 128 columns
+        const int cq = (warp - 2) >> 2;                     // which 64 columns
         const int row = m0 + 32 * quarter + lane;
         if (ok) {
-            for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
+            for (int c0 = 64 * cq; c0 < 64 * cq + 64; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
                 if (row < p.M) {
                     uint16_t* crow = p.C + (size_t)row * p.N + n0 + c0;
-                    if (n0 + c0 + 32 <= p.N && (p.N % 8) == 0) {
+                    if (n0 + c0 + 32 <= p.N) {
 #pragma unroll
                         for (int k = 0; k < 32; k += 8) {
                             uint4 o;
@@ -291,7 +301,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         // the issuer committed acc_full after its last MMA; wait for it (bounded)
         mbar_wait_bounded(acc_full, 0, kWaitLimitNs / 4);
         // and for copies still landing in the ring
-        for (int s = 0; s < kStages; ++s) mbar_wait_bounded(&full_tma[s], 0, kWaitLimitNs / 8);
+        for (int s = 0; s < kTmaStages; ++s) mbar_wait_bounded(&full_tma[s], 0, kWaitLimitNs / 8);
     }
     __syncthreads();
     if (warp == 1) {
@@ -303,7 +313,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
 template <bool SIGNED, bool HAS_ZP>
 int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
     auto kern = gemm_w4_tc_kernel<SIGNED, HAS_ZP>;
-    const size_t smem = 1024 + (size_t)kStages * kStageBytes + (3 * kStages + 1) * 8 + 16;
+    const size_t smem = 1024 + (size_t)kRingBytes + kBarriers * 8 + 16;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

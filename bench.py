@@ -139,6 +139,53 @@ def make_layer(rank, world, M, dev, gen):
     return layer
 
 
+def prefill_gemm(dev, M=4096, steps=5, warmup=3):
+    """Second half of the metric: the tcgen05 prefill GEMM at M = 4096 over the
+    seven projections of one Llama-3-8B layer (one step = all seven), timed
+    with CUDA events on the current stream; TFLOP/s = 2 M K N / time."""
+    from t4_cuda_b200 import ops
+    gen = torch.Generator(device=dev).manual_seed(11)
+    layer = {}
+    for name, K, N in PROJ:
+        W = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=gen)
+        S = (torch.randn((K // GROUP, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+        layer[name] = (W, S)
+    acts = {k: torch.randn((M, kk), device=dev, generator=gen).half() for k, kk in (("x", 4096), ("h", 14336))}
+
+    def step():
+        for name, K, N in PROJ:
+            ops.fused_w4a16_gemm_s4(acts["h"] if name == "down" else acts["x"], layer[name][0], layer[name][1], None)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    flops = sum(2.0 * M * K * N for _, K, N in PROJ)
+    per_shape = {}
+    for name, K, N in PROJ:
+        a = acts["h"] if name == "down" else acts["x"]
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(steps):
+            ops.fused_w4a16_gemm_s4(a, layer[name][0], layer[name][1], None)
+        f1.record()
+        f1.synchronize()
+        us = f0.elapsed_time(f1) * 1e3 / steps
+        per_shape[f"{name}_{K}x{N}"] = {"us": round(us, 2), "TFLOP/s": round(2.0 * M * K * N / us / 1e6, 1)}
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {"metric": "GEMM TFLOPS at M=4096", "value": round(tflops, 1), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 4), "steps": steps, "warmup": warmup,
+            "config": {"workload": "prefill: one Llama-3-8B layer, 7 projections at M=4096, s4 g128", "M": M},
+            "kernel": "gemm_w4_tc_kernel (tcgen05.mma kind::f16, 128x256 tiles, TMEM accumulator)",
+            "per_shape": per_shape}
+
+
 def run_ours(args):
     from t4_cuda_b200 import ops
     from t4_cuda_b200.shard import ShardedGroup, ShardedLinear
@@ -240,6 +287,11 @@ def run_ours(args):
             per_shape[f"{name}_{K}x{N}"] = {"us": round(us, 3), "GB/s": round(alg_bytes(M, K, N) / us / 1e3, 1)}
             del g
 
+    # ---- second half of the metric: prefill GEMM at M = 4096 (one GPU)
+    gemm = None
+    if world == 1 and not args.no_gemm:
+        gemm = prefill_gemm(dev)
+
     # ---- end to end through the public API, host buffers, copies timed
     pin = {a: t.cpu().pin_memory() for a, t in acts.items()}
     dev_in = {a: torch.empty_like(t) for a, t in acts.items()}
@@ -286,13 +338,13 @@ def run_ours(args):
     roof = None
     if world == 1:
         tr = traffic.get("decode_step")
-        roof = {"bound": "hbm", "kernel": "gemv_w4_kernel", "achieved": round(achieved, 1),
+        roof = {"bound": "hbm", "kernel": "gemv_w4_decode_kernel", "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
                 else "fallback 6650 GB/s",
                 "traffic": (tr / launches_per_step) if tr else None,
                 "algorithmic_bytes_per_launch": step_bytes / launches_per_step,
-                "note": "timed region holds only gemv_w4_kernel launches; duration per launch = region / launches"}
+                "note": "timed region holds only gemv_w4_decode_kernel launches; duration per launch = region / launches"}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
@@ -312,6 +364,13 @@ def run_ours(args):
         "roofline": roof,
         "clocks": clk.summary(),
     }
+    if gemm is not None:
+        pk = peaks["bf16_tflops"]
+        gemm["roofline"] = {"bound": "tensor", "achieved": gemm["value"], "peak": pk, "unit": "TFLOP/s",
+                            "frac": round(gemm["value"] / pk, 4),
+                            "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)" if peaks["source"] == "measured"
+                            else "fallback 1590 TFLOP/s", "traffic": None}
+        line["gemm"] = gemm
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
     print(json.dumps(line), flush=True)
@@ -387,6 +446,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--no-gemm", action="store_true", help="skip the M=4096 prefill GEMM half of the metric")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=1, help="activation rows (decode batch)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")

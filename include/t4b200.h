@@ -61,10 +61,12 @@ int t4b_device_error(void* stream, unsigned* out, int clear);
 
 /* Kernel selection for the W4A16 matmul (argument of t4b_set_gemv_kernel). */
 enum {
-    T4B_GEMV_AUTO = 0,     /* best kernel that applies: resident-activation decode kernel,
-                              then the TMA-streamed split-tile kernel, then generic          */
+    T4B_GEMV_AUTO = 0,     /* best kernel that applies: for M <= 16 the resident-activation
+                              decode kernel, then the TMA-streamed split-tile kernel; for
+                              M > 16 the tcgen05 GEMM (CTA pairs when M > 128); else generic */
     T4B_GEMV_GENERIC = 1,  /* always the generic register-streaming kernel (for comparison)  */
-    T4B_GEMV_STREAM = 2    /* the TMA-streamed split-tile kernel where it applies, else generic */
+    T4B_GEMV_STREAM = 2,   /* the TMA-streamed split-tile kernel where it applies, else generic */
+    T4B_GEMV_TC_SINGLE = 3 /* as AUTO, but M > 16 always on the single-CTA tcgen05 kernel     */
 };
 /* Sets the process-wide choice; returns the previous one (-1: bad argument).
  * No counterpart in the reference (it has a single kernel). */

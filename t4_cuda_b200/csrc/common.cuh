@@ -41,8 +41,9 @@ int decode_device_error(cudaStream_t stream, unsigned* out, bool clear);
 
 // Prefill GEMM on tcgen05 / TMEM (M > 16, K % 64 == 0, group % 64 == 0);
 // T4B_ERR_UNSUPPORTED (without launching) for shapes it does not take.
+// allow_pairs: M > 128 runs on CTA pairs (cta_group::2); else single CTAs.
 int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N, int K,
-               int group, cudaStream_t stream);
+               int group, bool allow_pairs, cudaStream_t stream);
 int gemm_tc_device_error(cudaStream_t stream, unsigned* out, bool clear);
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }

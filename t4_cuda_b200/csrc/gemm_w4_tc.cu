@@ -310,6 +310,324 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     }
 }
 
+// =============================================================================
+// CTA-pair variant (M > 128): a cluster of two CTAs on one TPC runs
+// tcgen05.mma.cta_group::2 with M = 256, N = 256 -- the pair computes a
+// 256 x 256 tile of C, each CTA holding its 128 rows of A and dequantizing 128
+// of the 256 weight columns (the MMA takes the B operand N-split across the
+// two CTAs' shared memory at the same offset).  Against the single-CTA
+// kernel this halves the dequant work and the shared-memory traffic of B per
+// SM (B is the largest operand there), which is what bounds that kernel.
+//
+//   warp 0      (both CTAs) one thread issues this CTA's TMA copies of a
+//               stage (A 128 x 64, packed words 8 x 128, one scale row) and
+//               signals this CTA's own "full" barrier -- no copy writes or
+//               signals the other CTA;
+//   warp 1      (both CTAs) allocates the pair's TMEM (cta_group::2); in the
+//               leader CTA one thread waits for the pair's B slot to be
+//               complete, issues the four K = 16 MMAs of the stage and commits
+//               them to the "done" barrier of the stage in BOTH CTAs (two
+//               commits, one per CTA, no multicast);
+//   warps 2..   dequantize this CTA's 128 columns into its B slot, then arrive
+//               on the LEADER's "B full" barrier (a cluster-scope remote arrive
+//               from the other CTA).  Their arrival also certifies the stage's
+//               A copy, which they waited for, so the issuer waits on one
+//               barrier per stage.  After the last stage they drain this CTA's
+//               128 accumulator rows from TMEM.
+// "done[s]" frees TMA slot s (stage i reuses it after stage i - kPairTmaStages)
+// and B slot (i - kPairBStages) % kPairBStages.
+namespace pair {
+
+constexpr int kRows = 128;                          // rows of A per CTA
+constexpr int kCols = 256;                          // columns of C per pair
+constexpr int kHalf = 128;                          // B columns per CTA
+constexpr int kTmaStages = 6;
+constexpr int kBStages = 4;
+constexpr int kDqWarps = 8;
+constexpr int kThreads = 64 + 32 * kDqWarps;
+constexpr int kWordsPerThread = 8 * kHalf / (32 * kDqWarps);   // packed words (of the 8 per column) per thread
+constexpr int kABytes = kRows * kBK * 2;            // 16 KB
+constexpr int kWBytes = (kBK / 8) * kHalf * 4;      // 4 KB
+constexpr int kSBytes = kHalf * 2;                  // 256 B
+constexpr int kStageBytes = 21 * 1024;              // A, packed, scales, zero points, padded so every A tile is 1024-aligned
+constexpr int kBBytes = kHalf * kBK * 2;            // 16 KB
+constexpr int kRingBytes = kTmaStages * kStageBytes + kBStages * kBBytes;
+constexpr int kBarriers = 2 * kTmaStages + kBStages + 1;
+static_assert(kWordsPerThread * 32 * kDqWarps == 8 * kHalf, "dequant split");
+static_assert(kTmaStages > kBStages, "done-barrier reuse argument needs more TMA stages than B stages");
+static_assert(kStageBytes % 1024 == 0 && kStageBytes >= kABytes + kWBytes + 2 * kSBytes, "stage layout");
+static_assert((kTmaStages * kStageBytes) % 1024 == 0 && kBBytes % 1024 == 0, "B slots 1024-aligned");
+
+// kind::f16, fp16 A/B K-major, fp32 accumulator, M = 256 (pair), N = 256.
+constexpr uint32_t kInstrDesc = (1u << 4) | ((uint32_t)(kCols >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of this CTA's shared variable `p` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+
+// Arrive on a barrier of either CTA of the pair (default .release.cta
+// semantics: the shared-memory writes it publishes are this CTA's own, made
+// visible to the tensor core's async proxy by fence.proxy.async beforehand; a
+// cluster-scope release here costs a memory barrier of ~900 cycles per stage).
+__device__ __forceinline__ void arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Bounded wait; the fast path is a single try_wait.
+__device__ __forceinline__ bool wait_pair(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) break;
+    }
+    *abort_flag = 1;
+    atomicOr(&g_gemm_tc_error, kErrTimeout);
+    return false;
+}
+
+__device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :
+        : "r"(tmem_d), "l"(da), "l"(db), "r"(kInstrDesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void commit_pair(uint32_t cluster_addr) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+
+template <bool SIGNED, bool HAS_ZP>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    // Same offsets in both CTAs: the MMA addresses the partner's operands by
+    // this CTA's shared-memory offsets.
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint8_t* bring = base + kTmaStages * kStageBytes;
+    uint64_t* full_tma = reinterpret_cast<uint64_t*>(base + kRingBytes);
+    uint64_t* done = full_tma + kTmaStages;
+    uint64_t* full_b = done + kTmaStages;            // used in the leader only
+    uint64_t* acc_full = full_b + kBStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();            // 0 = leader (issues the MMAs)
+    // 1-D grid of pairs (clusters of 2 along x), column tiles fastest
+    const int pair_id = blockIdx.x >> 1;
+    const int n_tiles = (p.N + kCols - 1) / kCols;
+    const int n0 = (pair_id % n_tiles) * kCols;      // pair's columns
+    const int nh = n0 + (int)rank * kHalf;           // this CTA's B columns
+    const int m0 = (pair_id / n_tiles) * (2 * kRows) + (int)rank * kRows;   // this CTA's rows
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTmaStages; ++s) {
+            mbar_init(&full_tma[s], 1);
+            mbar_init(&done[s], 1);              // one commit from the leader's issuer
+        }
+        for (int b = 0; b < kBStages; ++b) mbar_init(&full_b[b], 2 * kDqWarps);   // every dequant warp of the pair
+        mbar_init(acc_full, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&maps.a);
+        prefetch_tmap(&maps.w);
+        prefetch_tmap(&maps.s);
+        if constexpr (HAS_ZP) prefetch_tmap(&maps.z);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    cluster_sync_all();          // both CTAs' barriers initialised before any remote arrive or commit
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (each CTA loads only its own operands)
+        if (lane == 0) {
+            for (int i = 0; i < p.ksteps; ++i) {
+                const int s = i % kTmaStages;
+                if (i >= kTmaStages &&
+                    !wait_pair(&done[s], (uint32_t)(((i / kTmaStages) & 1) ^ 1), abort_flag))
+                    break;
+                uint8_t* st = base + s * kStageBytes;
+                const int srow = p.gw_steps ? i / p.gw_steps : 0;
+                mbar_arrive_expect_tx(&full_tma[s], kABytes + kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
+                tma_load_2d(st, &maps.a, i * kBK, m0, &full_tma[s]);
+                tma_load_2d(st + kABytes, &maps.w, nh, i * (kBK / 8), &full_tma[s]);
+                tma_load_2d(st + kABytes + kWBytes, &maps.s, nh, srow, &full_tma[s]);
+                if constexpr (HAS_ZP)
+                    tma_load_2d(st + kABytes + kWBytes + kSBytes, &maps.z, nh, srow, &full_tma[s]);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader CTA only)
+        if (rank == 0 && lane == 0) {
+            // cluster addresses of done[0] in each CTA; done[s] lies 8 s bytes further
+            const uint32_t done0 = map_to_rank(&done[0], 0), done1 = map_to_rank(&done[0], 1);
+            for (int i = 0; i < p.ksteps; ++i) {
+                const int s = i % kTmaStages, b = i % kBStages;
+                if (!wait_pair(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(base + s * kStageBytes);
+                const uint32_t b_addr = smem_addr(bring + b * kBBytes);
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk)
+                    mma_pair(tmem_d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
+                             (i > 0 || kk > 0) ? 1u : 0u);
+                commit_pair(done0 + (uint32_t)(s * 8));     // fire once these MMAs have read their operands
+                commit_pair(done1 + (uint32_t)(s * 8));
+            }
+            commit_pair(map_to_rank(acc_full, 0));     // fire once every MMA issued above has completed
+            commit_pair(map_to_rank(acc_full, 1));
+        }
+    } else {
+        // ---------------- dequant warps, then epilogue
+        const int t = threadIdx.x - 64;
+        const int n = t & (kHalf - 1);                       // column of this CTA's half
+        const int j0 = (t / kHalf) * kWordsPerThread;        // first word row of the K step
+        const uint32_t full_b_leader = map_to_rank(&full_b[0], 0);
+        for (int i = 0; i < p.ksteps; ++i) {
+            const int s = i % kTmaStages, b = i % kBStages;
+            if (!wait_pair(&full_tma[s], (uint32_t)((i / kTmaStages) & 1), abort_flag)) break;
+            if (i >= kBStages) {
+                const int r = i - kBStages;
+                if (!wait_pair(&done[r % kTmaStages], (uint32_t)((r / kTmaStages) & 1), abort_flag)) break;
+            }
+            const uint8_t* st = base + s * kStageBytes;
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + kABytes);
+            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kABytes + kWBytes);
+            uint8_t* bt = bring + b * kBBytes;
+            const uint16_t sbits = sp[n];
+            const uint32_t s2 = h2_dup(sbits);
+            float zf = 0.f, sf = 0.f;
+            if constexpr (HAS_ZP) {
+                zf = h_to_f(sp[kHalf + n]);
+                sf = h_to_f(sbits);
+            }
+#pragma unroll
+            for (int jj = 0; jj < kWordsPerThread; ++jj) {
+                const int j = j0 + jj;
+                const uint32_t w = wp[j * kHalf + n];
+                uint32_t q[4];
+                unpack_natural<SIGNED>(w, q);
+                uint4 o;
+                uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if constexpr (HAS_ZP) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[k]));
+                        ov[k] = f2_to_h2((f.x - zf) * sf, (f.y - zf) * sf);
+                    } else {
+                        ov[k] = h2_mul(q[k], s2);
+                    }
+                }
+                *reinterpret_cast<uint4*>(bt + n * 128 + ((j ^ (n & 7)) << 4)) = o;
+            }
+            fence_proxy_async_smem();      // generic-proxy writes of B before the MMA reads them
+            __syncwarp();
+            if (lane == 0) arrive_cluster(full_b_leader + (uint32_t)(b * 8));
+        }
+        // ---------------- epilogue: TMEM lanes 32 * (warp % 4) .. +31 = this CTA's rows
+        const bool ok = wait_pair(acc_full, 0, abort_flag);
+        tc_fence_after();
+        const int quarter = warp & 3;
+        constexpr int kColsPerWarp = kCols / (kDqWarps / 4);
+        const int cq = (warp - 2) >> 2;
+        const int row = m0 + 32 * quarter + lane;
+        if (ok) {
+            for (int c0 = kColsPerWarp * cq; c0 < kColsPerWarp * cq + kColsPerWarp; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+                if (row < p.M) {
+                    uint16_t* crow = p.C + (size_t)row * p.N + n0 + c0;
+                    if (n0 + c0 + 32 <= p.N) {
+#pragma unroll
+                        for (int k = 0; k < 32; k += 8) {
+                            uint4 o;
+                            o.x = f2_to_h2(__uint_as_float(v[k + 0]), __uint_as_float(v[k + 1]));
+                            o.y = f2_to_h2(__uint_as_float(v[k + 2]), __uint_as_float(v[k + 3]));
+                            o.z = f2_to_h2(__uint_as_float(v[k + 4]), __uint_as_float(v[k + 5]));
+                            o.w = f2_to_h2(__uint_as_float(v[k + 6]), __uint_as_float(v[k + 7]));
+                            *reinterpret_cast<uint4*>(crow + k) = o;
+                        }
+                    } else {
+                        for (int k = 0; k < 32; ++k)
+                            if (n0 + c0 + k < p.N) crow[k] = __half_as_ushort(__float2half_rn(__uint_as_float(v[k])));
+                    }
+                }
+            }
+        }
+    }
+
+    // ---------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag && threadIdx.x == 32) {
+        // the leader's issuer committed acc_full after its last MMA; wait for it (bounded)
+        mbar_wait_bounded(acc_full, 0, kWaitLimitNs / 4);
+        for (int s = 0; s < kTmaStages; ++s) mbar_wait_bounded(&full_tma[s], 0, kWaitLimitNs / 8);
+    }
+    __syncthreads();
+    cluster_sync_all();          // neither CTA frees TMEM or exits while the other may still signal it
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kCols));
+    }
+}
+
+template <bool SIGNED, bool HAS_ZP>
+int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
+    auto kern = gemm_w4_tc_pair_kernel<SIGNED, HAS_ZP>;
+    const size_t smem = 1024 + (size_t)kRingBytes + kBarriers * 8 + 16;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    const int pairs = ((p.N + kCols - 1) / kCols) * ((p.M + 2 * kRows - 1) / (2 * kRows));
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;      // the two CTAs of an MMA pair are adjacent along x
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    return check_launch();
+}
+
+}  // namespace pair
+
 template <bool SIGNED, bool HAS_ZP>
 int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
     auto kern = gemm_w4_tc_kernel<SIGNED, HAS_ZP>;
@@ -337,7 +655,7 @@ int gemm_tc_device_error(cudaStream_t stream, unsigned* out, bool clear) {
 }
 
 int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N, int K,
-               int group, cudaStream_t stream) {
+               int group, bool allow_pairs, cudaStream_t stream) {
     if (M <= 16 || (K % kBK) != 0 || (group % kBK) != 0 || (N % 8) != 0) return T4B_ERR_UNSUPPORTED;
     if (!aligned(A, 16) || !aligned(W, 16) || !aligned(S, 16) || (Z && !aligned(Z, 16)) || !aligned(C, 16))
         return T4B_ERR_UNSUPPORTED;
@@ -346,16 +664,23 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
     p.M = M; p.N = N; p.K = K;
     p.ksteps = K / kBK;
     p.gw_steps = (group >= K) ? 0 : group / kBK;
+    // M > 128: CTA pairs (each CTA dequantizes 128 of a pair's 256 columns)
+    const bool use_pair = M > kBM && allow_pairs;
+    const uint32_t wbox = use_pair ? pair::kHalf : kBN;
     GemmMaps maps;
     if (!make_tmap_2d_ex(&maps.a, true, A, (uint64_t)M, (uint64_t)K, kBM, kBK, 128, 256) ||
-        !make_tmap_2d_ex(&maps.w, false, W, (uint64_t)(K / 8), (uint64_t)N, kBK / 8, kBN, 0, 256) ||
-        !make_tmap_2d_ex(&maps.s, true, S, (uint64_t)(K / group), (uint64_t)N, 1, kBN, 0, 0))
+        !make_tmap_2d_ex(&maps.w, false, W, (uint64_t)(K / 8), (uint64_t)N, kBK / 8, wbox, 0, 256) ||
+        !make_tmap_2d_ex(&maps.s, true, S, (uint64_t)(K / group), (uint64_t)N, 1, wbox, 0, 0))
         return T4B_ERR_UNSUPPORTED;
     if (Z) {
-        if (!make_tmap_2d_ex(&maps.z, true, Z, (uint64_t)(K / group), (uint64_t)N, 1, kBN, 0, 0))
+        if (!make_tmap_2d_ex(&maps.z, true, Z, (uint64_t)(K / group), (uint64_t)N, 1, wbox, 0, 0))
             return T4B_ERR_UNSUPPORTED;
     } else {
         maps.z = maps.s;
+    }
+    if (use_pair) {
+        if (is_signed) return Z ? pair::launch<true, true>(maps, p, stream) : pair::launch<true, false>(maps, p, stream);
+        return Z ? pair::launch<false, true>(maps, p, stream) : pair::launch<false, false>(maps, p, stream);
     }
     if (is_signed) return Z ? launch<true, true>(maps, p, stream) : launch<true, false>(maps, p, stream);
     return Z ? launch<false, true>(maps, p, stream) : launch<false, false>(maps, p, stream);

@@ -283,15 +283,16 @@ int fused_gemm(const void* A, const void* W, const void* S, const void* Z, void*
     if (!aligned(A, 16) || !aligned(W, 4) || !aligned(S, 2) || !aligned(C, 2) || (Z && !aligned(Z, 2)))
         return T4B_ERR_MISALIGNED;
     const int choice = g_gemv_kernel.load();
-    if (choice == T4B_GEMV_AUTO && M > kStreamMaxM) {
-        const int st = gemm_w4_tc(SIGNED, A, W, S, Z, C, M, N, K, group, static_cast<cudaStream_t>(stream_));
+    if ((choice == T4B_GEMV_AUTO || choice == T4B_GEMV_TC_SINGLE) && M > kStreamMaxM) {
+        const int st = gemm_w4_tc(SIGNED, A, W, S, Z, C, M, N, K, group, choice == T4B_GEMV_AUTO,
+                                  static_cast<cudaStream_t>(stream_));
         if (st != T4B_ERR_UNSUPPORTED) return st;
     }
-    if (choice == T4B_GEMV_AUTO && M <= kStreamMaxM) {
+    if ((choice == T4B_GEMV_AUTO || choice == T4B_GEMV_TC_SINGLE) && M <= kStreamMaxM) {
         const int st = gemv_w4_decode(SIGNED, A, W, S, Z, C, M, N, K, group, static_cast<cudaStream_t>(stream_));
         if (st != T4B_ERR_UNSUPPORTED) return st;
     }
-    if ((choice == T4B_GEMV_AUTO || choice == T4B_GEMV_STREAM) && M <= kStreamMaxM) {
+    if ((choice == T4B_GEMV_AUTO || choice == T4B_GEMV_TC_SINGLE || choice == T4B_GEMV_STREAM) && M <= kStreamMaxM) {
         const int st = gemv_w4_stream(SIGNED, A, W, S, Z, C, M, N, K, group, static_cast<cudaStream_t>(stream_));
         if (st != T4B_ERR_UNSUPPORTED) return st;
     }
@@ -327,7 +328,8 @@ int fused_gemm(const void* A, const void* W, const void* S, const void* Z, void*
 extern "C" {
 
 int t4b_set_gemv_kernel(int which) {
-    if (which != T4B_GEMV_AUTO && which != T4B_GEMV_GENERIC && which != T4B_GEMV_STREAM) return -1;
+    if (which != T4B_GEMV_AUTO && which != T4B_GEMV_GENERIC && which != T4B_GEMV_STREAM && which != T4B_GEMV_TC_SINGLE)
+        return -1;
     return t4b::g_gemv_kernel.exchange(which);
 }
 

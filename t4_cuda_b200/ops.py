@@ -28,15 +28,16 @@ __all__ = [
     "set_gemv_kernel", "device_error",
 ]
 
-_GEMV_KERNELS = {"auto": 0, "generic": 1, "stream": 2}
+_GEMV_KERNELS = {"auto": 0, "generic": 1, "stream": 2, "tc_single": 3}
 
 
 def set_gemv_kernel(which="auto"):
     """Choose the W4A16 matmul kernel process-wide: "auto" (the best kernel that
-    applies: resident-activation decode kernel, then the TMA-streamed
-    split-tile kernel, then generic), "stream" (the split-tile kernel where it
-    applies) or "generic" (the register-streaming kernel).  Returns the
-    previous choice."""
+    applies: for M <= 16 the resident-activation decode kernel, then the
+    TMA-streamed split-tile kernel; for M > 16 the tcgen05 GEMM, on CTA pairs
+    when M > 128; else generic), "tc_single" (as "auto" but M > 16 always on
+    single-CTA tcgen05 tiles), "stream" (the split-tile kernel where it applies)
+    or "generic" (the register-streaming kernel).  Returns the previous choice."""
     _check(which in _GEMV_KERNELS, f"which must be one of {sorted(_GEMV_KERNELS)}")
     prev = _lib.load().t4b_set_gemv_kernel(_GEMV_KERNELS[which])
     return {v: k for k, v in _GEMV_KERNELS.items()}[prev]

@@ -114,6 +114,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
 
 // Bounded wait; on timeout records the error and raises the CTA's abort flag.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (mbar_wait_bounded(bar, parity, kWaitLimitNs)) return true;
     *abort_flag = 1;
@@ -204,12 +205,17 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     } else if (warp == 1) {
         // ---------------- MMA issuer
         if (lane == 0) {
+            // The dequant warps arrive on full_b[b] only after waiting for the
+            // stage's TMA copy, so full_b alone certifies both operands.
+            bool ready = mbar_try_wait(&full_b[0], 0);
             for (int i = 0; i < p.ksteps; ++i) {
                 const int s = i % kTmaStages, b = i % kBStages;
-                if (!wait_or_abort(&full_tma[s], (uint32_t)((i / kTmaStages) & 1), abort_flag) ||
-                    !wait_or_abort(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag))
-                    break;
-                tc_fence_after();
+                if (!ready && !wait_or_abort(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag)) break;
+                // peek at the next stage while this one's MMAs queue (no tcgen05 fence
+                // per stage: the barrier orders the operands, and a fence here would
+                // hold the issuer until the queued MMAs drain)
+                ready = (i + 1 < p.ksteps) &&
+                        mbar_try_wait(&full_b[(i + 1) % kBStages], (uint32_t)(((i + 1) / kBStages) & 1));
                 const uint32_t a_addr = smem_addr(base + s * kTmaStageBytes);
                 const uint32_t b_addr = smem_addr(bring + b * kBBytes);
 #pragma unroll
@@ -487,10 +493,15 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
         if (rank == 0 && lane == 0) {
             // cluster addresses of done[0] in each CTA; done[s] lies 8 s bytes further
             const uint32_t done0 = map_to_rank(&done[0], 0), done1 = map_to_rank(&done[0], 1);
+            bool ready = mbar_try_wait(&full_b[0], 0);
             for (int i = 0; i < p.ksteps; ++i) {
                 const int s = i % kTmaStages, b = i % kBStages;
-                if (!wait_pair(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag)) break;
-                tc_fence_after();
+                if (!ready && !wait_pair(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag)) break;
+                // peek at the next stage while this one's MMAs queue (no tcgen05 fence
+                // per stage: the barrier orders the operands, and a fence here would
+                // hold the issuer until the queued MMAs drain)
+                ready = (i + 1 < p.ksteps) &&
+                        mbar_try_wait(&full_b[(i + 1) % kBStages], (uint32_t)(((i + 1) / kBStages) & 1));
                 const uint32_t a_addr = smem_addr(base + s * kStageBytes);
                 const uint32_t b_addr = smem_addr(bring + b * kBBytes);
 #pragma unroll

@@ -58,14 +58,15 @@ def load_peaks():
 
 
 def load_traffic():
-    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary
-    (profiles/gemv_w4_decode.md, line 'traffic_bytes_per_launch <shape> <bytes>')."""
+    """DRAM bytes of one decode step from the committed ncu summary
+    (profiles/gemv_w4_decode.md, line 'traffic_bytes_per_step <name> <bytes>');
+    the roofline reports it per launch (divided by the launches of a step)."""
     p = os.path.join(ROOT, "profiles", "gemv_w4_decode.md")
     out = {}
     if os.path.exists(p):
         for line in open(p):
             parts = line.strip().strip("`").split()
-            if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch":
+            if len(parts) == 3 and parts[0] == "traffic_bytes_per_step":
                 out[parts[1]] = float(parts[2])
     return out
 
@@ -441,6 +442,39 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_case(spec, launches=6):
+    """Profiling driver (no JSON line): a few launches of ONE kernel on one
+    case, for ncu captures of a single kernel.
+      decode:K:N:M  s4 group-128 GEMV/skinny GEMM, weights rotating through a
+                    pool of >= 4x L2 so every launch reads them from HBM
+      gemm:M:K:N    s4 group-128 prefill GEMM (tcgen05)"""
+    from t4_cuda_b200 import ops
+    kind, *dims = spec.split(":")
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    if kind == "decode":
+        K, N, M = (int(x) for x in dims)
+        l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+        pool = max(4, (4 * l2) // (K * N // 2) + 1)
+        Ws = [torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=gen)
+              for _ in range(pool)]
+    elif kind == "gemm":
+        M, K, N = (int(x) for x in dims)
+        Ws = [torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=gen)]
+    else:
+        raise SystemExit(f"unknown case {spec!r}")
+    S = (torch.randn((K // GROUP, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+    A = torch.randn((M, K), device=dev, generator=gen).half()
+    for i in range(launches):
+        C = ops.fused_w4a16_gemm_s4(A, Ws[i % len(Ws)], S, None)
+    torch.cuda.synchronize()
+    err = ops.device_error(dev)
+    print(f"case {spec}: {launches} launches, mean |C| {float(C.float().abs().mean()):.4f}, device error {err}")
+    if err:
+        raise SystemExit(1)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -451,7 +485,12 @@ def main():
     ap.add_argument("--m", type=int, default=1, help="activation rows (decode batch)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", help="profiling driver: decode:K:N:M or gemm:M:K:N (a few launches, no JSON)")
+    ap.add_argument("--launches", type=int, default=6, help="launches for --case")
     args = ap.parse_args()
+    if args.case:
+        run_case(args.case, args.launches)
+        return
     args.warmup = max(3, args.warmup)     # at least 3 untimed warm-up steps
     if args.impl == "reference":
         run_reference(args)

@@ -23,7 +23,10 @@
 //   All of it is constant data, so the first stages are issued at kernel
 //   entry, before griddepcontrol.wait, and stream in while the previous
 //   kernel in the stream drains (two CTAs fit on an SM: one computing, one
-//   prefetching).  Whichever warp finishes a stage last refills its slot.
+//   prefetching).  A dedicated producer warp refills the slots: a copy
+//   issue can stall for hundreds of cycles while the copy engine is busy, and
+//   a math warp doing it would put that stall on every stage's critical path.
+//   The math warps release a slot by arriving on its "empty" barrier.
 //
 // Activations
 //   After griddepcontrol.wait the CTA copies A into shared memory once, as one
@@ -57,8 +60,8 @@ constexpr unsigned kErrTimeout = 1u;
 
 template <int MT>
 struct Shape {
-    static constexpr int kWarps = (MT == 1) ? 16 : 8;
-    static constexpr int kThreads = 32 * kWarps;
+    static constexpr int kWarps = (MT == 1) ? 16 : 8;          // consumer (math) warps
+    static constexpr int kThreads = 32 * (kWarps + 1);         // + one producer warp
     static constexpr int kWeightBytes = kWarps * 2048;         // packed words per stage
     static constexpr int kRowsNarrow = 16 * kWarps;            // stage rows, 1 warp column (1-2 tiles)
     static constexpr int kRowsWide = 8 * kWarps;               // stage rows, 2 warp columns (3-4 tiles)
@@ -235,7 +238,6 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
 gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p) {
     using S = Shape<MT>;
     constexpr int kWarps = S::kWarps;
-    constexpr int kThreads = S::kThreads;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned ring (pointer arithmetic on smem_raw keeps the
     // compiler aware that every access below is to shared memory)
@@ -244,33 +246,61 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     float* sums = reinterpret_cast<float*>(act + p.act_bytes);
     float* red = sums + p.sum_floats;
     uint64_t* full = reinterpret_cast<uint64_t*>(red + p.red_floats);
-    int* readers = reinterpret_cast<int*>(full + kMaxStages);
-    volatile int* sflag = reinterpret_cast<volatile int*>(readers + kMaxStages);   // [0] abort, [1] stages issued
+    uint64_t* empty = full + kMaxStages;       // one arrival per math warp
+    uint64_t* prep_done = empty + kMaxStages;  // the activations are in place
+    volatile int* sflag = reinterpret_cast<volatile int*>(prep_done + 1);   // [0] abort, [1] stages issued
 
     pdl_launch_dependents();
     const CtaPlan q = cta_plan<MT>(p);
     const int tid = threadIdx.x;
+    constexpr int kMathThreads = 32 * kWarps;
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
-            readers[s] = 0;
+            mbar_init(&empty[s], kWarps);
         }
+        mbar_init(prep_done, 1);
         sflag[0] = 0;
+        sflag[1] = 0;
         fence_barrier_init();
-        prefetch_tmap(&maps.w_wide);
-        prefetch_tmap(&maps.w_narrow);
-        prefetch_tmap(&maps.s_wide);
-        prefetch_tmap(&maps.s_narrow);
-        if constexpr (HAS_ZP) {
-            prefetch_tmap(&maps.z_wide);
-            prefetch_tmap(&maps.z_narrow);
-        }
-        // weights, scales and zero points are never written by a kernel of
-        // this library, so they may be fetched before the previous kernel ends
-        const int early = q.total < p.early ? q.total : p.early;
-        for (int s = 0; s < early; ++s) issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, s, s);
-        sflag[1] = early;
     }
+    __syncthreads();
+
+    if (tid >= kMathThreads) {
+        // ---------------- producer warp: every TMA copy of the ring
+        if (tid == kMathThreads) {
+            prefetch_tmap(&maps.w_wide);
+            prefetch_tmap(&maps.w_narrow);
+            prefetch_tmap(&maps.s_wide);
+            prefetch_tmap(&maps.s_narrow);
+            if constexpr (HAS_ZP) {
+                prefetch_tmap(&maps.z_wide);
+                prefetch_tmap(&maps.z_narrow);
+            }
+            // weights, scales and zero points are never written by a kernel of
+            // this library, so they may be fetched before the previous kernel ends
+            const int early = q.total < p.early ? q.total : p.early;
+            for (int s = 0; s < early; ++s) issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, s, s);
+            sflag[1] = early;
+            // The rest of the ring only once the activations are in: their
+            // loads are on the critical path and should not queue behind this
+            // SM's weight stream.
+            bool ok = mbar_wait_bounded(prep_done, 0, kWaitLimitNs);
+            for (int i = early; ok && i < q.total; ++i) {
+                const int slot = i % p.stages;
+                if (i >= p.stages && !mbar_wait_bounded(&empty[slot], (uint32_t)(((i / p.stages) & 1) ^ 1), kWaitLimitNs))
+                    ok = false;
+                if (!ok || sflag[0]) break;
+                fence_proxy_async_smem();     // the math warps' reads of the slot before the copy overwrites it
+                issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, i, slot);
+                sflag[1] = i + 1;
+            }
+            if (!ok) {
+                sflag[0] = 1;
+                atomicOr(&g_decode_error, kErrTimeout);
+            }
+        }
+    } else {
     pdl_wait_prior_grid();     // A and C may belong to the previous kernel
 
     // ---- resident activations: permuted records + flush-block sums.  Every
@@ -281,11 +311,11 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
         const int MB = 8 * MT;
         const int items = p.M * p.KWp;      // a multiple of 128: every test below is uniform per warp
         const uint32_t pitch = (uint32_t)(p.KWp + 2);
-        for (int base = 0; base < items; base += kThreads * kPrep) {
+        for (int base = 0; base < items; base += kMathThreads * kPrep) {
             uint4 v[kPrep];
 #pragma unroll
             for (int k = 0; k < kPrep; ++k) {
-                const int it = base + k * kThreads + tid;
+                const int it = base + k * kMathThreads + tid;
                 const int m = (int)fdiv((uint32_t)it, p.kwdiv);
                 const int kw = it - m * p.KWp;
                 v[k] = make_uint4(0, 0, 0, 0);
@@ -294,7 +324,7 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
             }
 #pragma unroll
             for (int k = 0; k < kPrep; ++k) {
-                const int it = base + k * kThreads + tid;
+                const int it = base + k * kMathThreads + tid;
                 if (it >= items) continue;      // uniform per warp (the shuffles below need all 32 lanes)
                 const int m = (int)fdiv((uint32_t)it, p.kwdiv);
                 const int kw = it - m * p.KWp;
@@ -316,19 +346,11 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
                 if ((kw & (p.fb - 1)) == 0) sums[(kw / p.fb) * MB + m] = s;
             }
         }
-        for (int idx = tid; idx < p.sum_floats; idx += kThreads)
+        for (int idx = tid; idx < p.sum_floats; idx += kMathThreads)
             if ((idx & (MB - 1)) >= p.M) sums[idx] = 0.f;
     }
-    __syncthreads();
-    if (tid == 0) {
-        // The rest of the ring, issued only now: the activation loads above
-        // were on the critical path and should not have queued behind this
-        // SM's weight stream (and an issue that stalls on a busy copy engine
-        // no longer holds up the whole CTA).
-        const int first = q.total < p.stages ? q.total : p.stages;
-        for (int s = sflag[1]; s < first; ++s) issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, s, s);
-        sflag[1] = first;
-    }
+    named_barrier(1, kMathThreads);
+    if (tid == 0) mbar_arrive(prep_done);
 
     const int warp = tid >> 5, lane = tid & 31;
     const int r = lane >> 2, c = lane & 3;
@@ -441,20 +463,9 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
                 }
             }
             // Every lane's reads of this slot are complete (their results fed
-            // the MMAs above); the last warp to get here refills the slot.
+            // the MMAs above): release it to the producer.
             __syncwarp();
-            if (lane == 0) {
-                __threadfence_block();   // this warp's reads of the slot before the count (release)
-                if (atomicAdd(&readers[slot], 1) == kWarps - 1) {
-                    readers[slot] = 0;
-                    const int nxt = i + p.stages;
-                    if (nxt < q.total && !sflag[0]) {
-                        fence_proxy_async_smem();
-                        issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, nxt, slot);
-                        sflag[1] = nxt + 1;
-                    }
-                }
-            }
+            if (lane == 0) mbar_arrive(&empty[slot]);
             if (++slot == p.stages) {
                 slot = 0;
                 phase ^= 1u;
@@ -474,7 +485,7 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
                     if (m < M) red[(warp * 32 + col) * M + m] = acc[mt][X][e];
                     acc[mt][X][e] = 0.f;
                 }
-        __syncthreads();
+        named_barrier(1, kMathThreads);
         const int col_base = kBoxCols * (q.t0 + 4 * g);
         int ncols = kBoxCols * nt;
         if (col_base + ncols > p.N) ncols = p.N - col_base;
@@ -487,10 +498,12 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
                 p.C[(size_t)m * p.N + col_base + col] = __half_as_ushort(__float2half_rn(v));
             }
         }
-        __syncthreads();
+        named_barrier(1, kMathThreads);
     }
+    }   // math warps
 
-    if (aborted && tid == 0) {
+    __syncthreads();
+    if (sflag[0] && tid == 0) {
         // do not leave while copies may still be landing in this CTA's memory
         const int issued = sflag[1];
         for (int j = (issued > p.stages ? issued - p.stages : 0); j < issued; ++j)
@@ -608,7 +621,7 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
     p.kwdiv = make_fastdiv((uint32_t)p.KWp);
     const int weight_bytes = warps * 2048;
     p.slot_bytes = (weight_bytes + p.s_bytes * (Z ? 2 : 1) + 1023) / 1024 * 1024;
-    const size_t fixed = 1024 + (size_t)p.act_bytes + 4 * (size_t)(p.sum_floats + p.red_floats) + kMaxStages * 12 + 16;
+    const size_t fixed = 1024 + (size_t)p.act_bytes + 4 * (size_t)(p.sum_floats + p.red_floats) + kMaxStages * 16 + 8 + 16;
     // two CTAs per SM (one computing, one prefetching the next kernel's
     // stages) when the ring still gets 2+ stages; else one CTA, deeper ring
     size_t two = 0, one = 0;

@@ -86,9 +86,11 @@ class ShardedGroup:
         M = locals_[0].size(0)
         widths = [t.size(1) for t in locals_]
         packed = torch.cat(locals_, dim=1) if len(locals_) > 1 else locals_[0]
-        gathered = torch.empty((self.world, M, packed.size(1)), dtype=packed.dtype, device=packed.device)
+        # gathered flat as [G * M, w] (rank-major), the form every backend
+        # accepts for all_gather_into_tensor, then viewed as [G, M, w]
+        gathered = torch.empty((self.world * M, packed.size(1)), dtype=packed.dtype, device=packed.device)
         dist.all_gather_into_tensor(gathered, packed.contiguous(), group=self.pg)
-        return unpack_gathered(gathered, widths)
+        return unpack_gathered(gathered.view(self.world, M, packed.size(1)), widths)
 
 
 def unpack_gathered(gathered, widths):

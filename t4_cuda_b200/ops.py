@@ -91,7 +91,8 @@ def _mode(mode):
 
 def _aligned16(t):
     """Contiguous tensor whose data pointer is 16-byte aligned (copy if not)."""
-    t = t.contiguous()
+    if not t.is_contiguous():
+        t = t.contiguous()
     if t.data_ptr() % 16:
         t = t.clone()
     return t
@@ -173,52 +174,94 @@ def dequantize_fp8(packed_weights, scales, mode="contract"):
 # --------------------------------------------------------------- fused GEMM
 def _group_rows(t, N, K, what):
     """(N,) / (1, N) / (G, N) -> number of rows G, with checks."""
-    _check(t.dim() in (1, 2), f"{what} must be 1-D (N,) or 2-D (K/group, N)")
-    if t.dim() == 1:
-        _check(t.numel() == N, f"{what} of shape (N,) must have N={N} elements, got {t.numel()}")
+    d = t.dim()
+    if d == 1:
+        if t.numel() != N:
+            _fail(f"{what} of shape (N,) must have N={N} elements, got {t.numel()}")
         return 1
-    _check(t.size(1) == N, f"{what} must have N={N} columns, got {t.size(1)}")
+    if d != 2:
+        _fail(f"{what} must be 1-D (N,) or 2-D (K/group, N)")
+    if t.size(1) != N:
+        _fail(f"{what} must have N={N} columns, got {t.size(1)}")
     G = t.size(0)
-    _check(G >= 1 and K % G == 0, f"{what}: {G} groups must divide K={K}")
-    gs = K // G
-    _check(gs % 8 == 0, f"{what}: group size K/{G}={gs} must be a multiple of 8")
+    if G < 1 or K % G:
+        _fail(f"{what}: {G} groups must divide K={K}")
+    if (K // G) % 8:
+        _fail(f"{what}: group size K/{G}={K // G} must be a multiple of 8")
     return G
 
 
+_FN = {}      # C entry points by name (ctypes function objects, looked up once)
+
+
+def _entry(name):
+    fn = _FN.get(name)
+    if fn is None:
+        fn = _FN[name] = getattr(_lib.load(), name)
+    return fn
+
+
+def _fail(msg):
+    raise RuntimeError(msg)
+
+
 def _fused(name, A, W_packed, scales, zero_points):
-    _check(A.is_cuda, "A must be a CUDA tensor")
-    _check(W_packed.is_cuda, "W_packed must be a CUDA tensor")
-    _check(scales.is_cuda, "scales must be a CUDA tensor")
+    # The decode path calls this once per projection per token, so the host
+    # work is kept short: the same checks as bindings.cpp:64-132 in the same
+    # order, with messages formatted only on failure.
+    if not A.is_cuda:
+        _fail("A must be a CUDA tensor")
+    if not W_packed.is_cuda:
+        _fail("W_packed must be a CUDA tensor")
+    if not scales.is_cuda:
+        _fail("scales must be a CUDA tensor")
     has_zp = zero_points is not None and zero_points.numel() > 0
     if has_zp:
-        _check(zero_points.is_cuda, "zero_points must be a CUDA tensor")
-        _check(zero_points.dtype == torch.float16, "zero_points must be FP16")
-    _check(A.dtype == torch.float16, "A must be FP16")
-    _check(W_packed.dtype == torch.int32, "W_packed must be Int32")
-    _check(scales.dtype == torch.float16, "scales must be FP16")
-    _check(A.dim() == 2, "A must be a 2-D (M, K) tensor")
-    _check(W_packed.dim() == 2, "W_packed must be a 2-D (K/8, N) tensor")
+        if not zero_points.is_cuda:
+            _fail("zero_points must be a CUDA tensor")
+        if zero_points.dtype != torch.float16:
+            _fail("zero_points must be FP16")
+    if A.dtype != torch.float16:
+        _fail("A must be FP16")
+    if W_packed.dtype != torch.int32:
+        _fail("W_packed must be Int32")
+    if scales.dtype != torch.float16:
+        _fail("scales must be FP16")
+    if A.dim() != 2:
+        _fail("A must be a 2-D (M, K) tensor")
+    if W_packed.dim() != 2:
+        _fail("W_packed must be a 2-D (K/8, N) tensor")
     dev = A.device
-    _check(W_packed.device == dev and scales.device == dev and (not has_zp or zero_points.device == dev),
-           "all tensors must be on the same device")
+    if W_packed.device != dev or scales.device != dev or (has_zp and zero_points.device != dev):
+        _fail("all tensors must be on the same device")
     M, K = A.shape
     N = W_packed.size(1)
-    _check(M > 0 and N > 0 and K > 0, "Dimensions M, N, K must be positive")
-    _check(K % 8 == 0, "K must be a multiple of 8 (8 INT4 values per int32 word)")
-    _check(W_packed.size(0) == K // 8, f"W_packed must have K/8={K // 8} rows, got {W_packed.size(0)}")
+    if M <= 0 or N <= 0 or K <= 0:
+        _fail("Dimensions M, N, K must be positive")
+    if K % 8:
+        _fail("K must be a multiple of 8 (8 INT4 values per int32 word)")
+    if W_packed.size(0) != K // 8:
+        _fail(f"W_packed must have K/8={K // 8} rows, got {W_packed.size(0)}")
     G = _group_rows(scales, N, K, "scales")
-    if has_zp:
-        _check(_group_rows(zero_points, N, K, "zero_points") == G, "zero_points must have the same shape as scales")
+    if has_zp and _group_rows(zero_points, N, K, "zero_points") != G:
+        _fail("zero_points must have the same shape as scales")
     A_ = _aligned16(A)
-    W_ = W_packed.contiguous()
-    S_ = scales.contiguous()
-    Z_ = zero_points.contiguous() if has_zp else None
+    W_ = W_packed if W_packed.is_contiguous() else W_packed.contiguous()
+    S_ = scales if scales.is_contiguous() else scales.contiguous()
+    Z_ = (zero_points if zero_points.is_contiguous() else zero_points.contiguous()) if has_zp else None
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
-    with _on_device(dev):
-        st = getattr(_lib.load(), name)(A_.data_ptr(), W_.data_ptr(), S_.data_ptr(),
-                                        Z_.data_ptr() if Z_ is not None else None, C.data_ptr(),
-                                        M, N, K, K // G, _stream_ptr(dev))
-    _lib.check(st, name)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    cur = torch.cuda.current_device()
+    if cur != idx:
+        torch.cuda.set_device(idx)
+    try:
+        st = _entry(name)(A_.data_ptr(), W_.data_ptr(), S_.data_ptr(), Z_.data_ptr() if Z_ is not None else None,
+                          C.data_ptr(), M, N, K, K // G, torch._C._cuda_getCurrentRawStream(idx))
+    finally:
+        if cur != idx:
+            torch.cuda.set_device(cur)
+    if st:
+        _lib.check(st, name)
     return C
 
 

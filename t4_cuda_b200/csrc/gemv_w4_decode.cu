@@ -301,6 +301,66 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
             }
         }
     } else {
+    // ---- per-lane constants and the offsets of the first tile group: none of
+    // it depends on the previous kernel, so the math warps compute it while
+    // that kernel drains instead of after the activations are in.
+    const int warp = tid >> 5, lane = tid & 31;
+    const int r = lane >> 2, c = lane & 3;
+    const int bb = r & 1;                     // which of the warp's two boxes
+    const int L = (r >> 1) ^ (r & 1);         // 16-byte chunk (4 columns) of that box
+    const uint32_t ring_a = smem_addr(ring);
+    const uint32_t act_a = smem_addr(act);
+    const uint32_t sum_lane = smem_addr(sums) + (uint32_t)(2 * c) * 4;
+    const uint32_t pitch16 = (uint32_t)(p.KWp + 2) * 16;
+    constexpr bool fb8 = FB8;     // 8-row flush blocks (group 64), else 16
+
+    // Offsets of tile group g for this lane.  Loads are unconditional (a guard
+    // around inline asm becomes a branch that splits the stage into small
+    // scheduling regions): a lane whose box lies past the group's last tile
+    // reads another box of the slot, and a lane past the last batch row reads
+    // row M-1; both only feed MMA rows / columns that are never stored.
+    int nt, nwc, rbs, rows, nst, kw_lane;
+    uint32_t woff[4], aoff[MT][4], soff[2];
+    auto setup_group = [&](int g) {
+        nt = (g < q.ng - 1) ? 4 : q.nt_last;
+        nwc = (nt + 1) >> 1;                      // warp columns (32 columns each)
+        rbs = kWarps / nwc;                       // 16-row blocks per stage
+        rows = 16 * rbs;
+        nst = (nwc == 2) ? p.s_wide : p.s_narrow;
+        const int wc = (nwc == 2) ? warp / (kWarps / 2) : 0;
+        const int rb = warp - wc * rbs;           // 16-row block of the stage
+        const int box = 2 * wc + bb;
+        kw_lane = 16 * rb;                        // first word row of this warp in a stage
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int row = kw_lane + row_of(j, c);
+            woff[j] = (uint32_t)(box * rows * 64 + row * 64) + (uint32_t)((L ^ ((row >> 1) & 3)) << 4);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const int m = min(r + 8 * mt, p.M - 1);
+                aoff[mt][j] = act_a + (uint32_t)m * pitch16 + (uint32_t)row * 16;
+            }
+        }
+        // scale row of this warp's flush blocks (rows kw_lane + 8h of the stage);
+        // a scale box row holds the group's 64 (wide) or 32 (narrow) columns
+        const int srow_bytes = (nwc == 2) ? 128 : 64;
+        const bool per_row = p.gw_shift >= 0 && p.gw < rows;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int srow = per_row ? ((kw_lane + 8 * h) >> p.gw_shift) : 0;
+            soff[h] = (uint32_t)(S::kWeightBytes + srow * srow_bytes + (16 * box + 4 * L) * 2);
+        }
+    };
+    setup_group(0);
+
+    float acc[MT][2][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int X = 0; X < 2; ++X)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][X][e] = 0.f;
+
     pdl_wait_prior_grid();     // A and C may belong to the previous kernel
 
     // ---- resident activations: permuted records + flush-block sums.  Every
@@ -352,63 +412,11 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     named_barrier(1, kMathThreads);
     if (tid == 0) mbar_arrive(prep_done);
 
-    const int warp = tid >> 5, lane = tid & 31;
-    const int r = lane >> 2, c = lane & 3;
-    const int bb = r & 1;                     // which of the warp's two boxes
-    const int L = (r >> 1) ^ (r & 1);         // 16-byte chunk (4 columns) of that box
-    const uint32_t ring_a = smem_addr(ring);
-    const uint32_t act_a = smem_addr(act);
-    const uint32_t sum_lane = smem_addr(sums) + (uint32_t)(2 * c) * 4;
-    const uint32_t pitch16 = (uint32_t)(p.KWp + 2) * 16;
-    constexpr bool fb8 = FB8;     // 8-row flush blocks (group 64), else 16
-
-    float acc[MT][2][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int X = 0; X < 2; ++X)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[mt][X][e] = 0.f;
-
     bool aborted = false;
     int i = 0, slot = 0;
     uint32_t phase = 0;
     for (int g = 0; g < q.ng; ++g) {
-        const int nt = (g < q.ng - 1) ? 4 : q.nt_last;
-        const int nwc = (nt + 1) >> 1;            // warp columns (32 columns each)
-        const int rbs = kWarps / nwc;             // 16-row blocks per stage
-        const int rows = 16 * rbs;
-        const int nst = (nwc == 2) ? p.s_wide : p.s_narrow;
-        const int wc = (nwc == 2) ? warp / (kWarps / 2) : 0;
-        const int rb = warp - wc * rbs;           // 16-row block of the stage
-        // Loads below are unconditional (a guard around inline asm becomes a
-        // branch that splits the stage into small scheduling regions).  A
-        // lane whose box lies past the group's last tile reads another box of
-        // the slot, and a lane past the last batch row reads row M-1: both
-        // only feed MMA rows / columns that are never stored.
-        const int box = 2 * wc + bb;
-        const int kw_lane = 16 * rb;              // first word row of this warp in a stage
-        uint32_t woff[4], aoff[MT][4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int row = kw_lane + row_of(j, c);
-            woff[j] = (uint32_t)(box * rows * 64 + row * 64) + (uint32_t)((L ^ ((row >> 1) & 3)) << 4);
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                const int m = min(r + 8 * mt, p.M - 1);
-                aoff[mt][j] = act_a + (uint32_t)m * pitch16 + (uint32_t)row * 16;
-            }
-        }
-        // scale row of this warp's flush blocks (rows kw_lane + 8h of the stage);
-        // a scale box row holds the group's 64 (wide) or 32 (narrow) columns
-        const int srow_bytes = (nwc == 2) ? 128 : 64;
-        const bool per_row = p.gw_shift >= 0 && p.gw < rows;
-        uint32_t soff[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int srow = per_row ? ((kw_lane + 8 * h) >> p.gw_shift) : 0;
-            soff[h] = (uint32_t)(S::kWeightBytes + srow * srow_bytes + (16 * box + 4 * L) * 2);
-        }
+        if (g > 0) setup_group(g);
         const uint32_t zdelta = (uint32_t)p.s_bytes;
 
         for (int ks = 0; ks < nst; ++ks, ++i) {

@@ -233,8 +233,13 @@ __device__ __forceinline__ void flush(float (&acc)[MT][2][4], const float (&dg)[
     }
 }
 
-template <int MT, bool SIGNED, bool HAS_ZP, bool FB8>
-__global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
+// MINB: CTAs per SM the register budget is sized for.  2 leaves room for the
+// next kernel's CTA to start early (programmatic dependent launch) on every
+// SM; 1 gives each thread twice the registers, which schedules the math
+// better, and is used when the grid covers at most half the SMs -- the next
+// kernel then starts early on the others.
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int MINB>
+__global__ void __launch_bounds__(Shape<MT>::kThreads, MINB)
 gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p) {
     using S = Shape<MT>;
     constexpr int kWarps = S::kWarps;
@@ -519,10 +524,10 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     }
 }
 
-template <int MT, bool SIGNED, bool HAS_ZP, bool FB8>
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int MINB>
 int launch(const DecodeMaps& maps, const DecodeParams& p, size_t smem,
            cudaStream_t stream) {
-    auto kern = gemv_w4_decode_kernel<MT, SIGNED, HAS_ZP, FB8>;
+    auto kern = gemv_w4_decode_kernel<MT, SIGNED, HAS_ZP, FB8, MINB>;
     static int configured = 0;   // largest dynamic shared memory set so far for this instantiation
     if ((int)smem > configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -544,21 +549,26 @@ int launch(const DecodeMaps& maps, const DecodeParams& p, size_t smem,
     return T4B_OK;
 }
 
-template <int MT, bool SIGNED>
+template <int MT, bool SIGNED, int MINB>
 int dispatch_zp(bool zp, bool fb8, const DecodeMaps& maps, const DecodeParams& p, size_t smem,
                 cudaStream_t stream) {
-    if (zp) return fb8 ? launch<MT, SIGNED, true, true>(maps, p, smem, stream)
-                       : launch<MT, SIGNED, true, false>(maps, p, smem, stream);
-    return fb8 ? launch<MT, SIGNED, false, true>(maps, p, smem, stream)
-               : launch<MT, SIGNED, false, false>(maps, p, smem, stream);
+    if (zp) return fb8 ? launch<MT, SIGNED, true, true, MINB>(maps, p, smem, stream)
+                       : launch<MT, SIGNED, true, false, MINB>(maps, p, smem, stream);
+    return fb8 ? launch<MT, SIGNED, false, true, MINB>(maps, p, smem, stream)
+               : launch<MT, SIGNED, false, false, MINB>(maps, p, smem, stream);
 }
 
-int dispatch(bool is_signed, bool zp, bool fb8, int MT, const DecodeMaps& maps, const DecodeParams& p, size_t smem,
-             cudaStream_t stream) {
-    if (MT == 1) return is_signed ? dispatch_zp<1, true>(zp, fb8, maps, p, smem, stream)
-                                  : dispatch_zp<1, false>(zp, fb8, maps, p, smem, stream);
-    return is_signed ? dispatch_zp<2, true>(zp, fb8, maps, p, smem, stream)
-                     : dispatch_zp<2, false>(zp, fb8, maps, p, smem, stream);
+int dispatch(bool is_signed, bool zp, bool fb8, int MT, bool few_ctas, const DecodeMaps& maps, const DecodeParams& p,
+             size_t smem, cudaStream_t stream) {
+    if (MT == 1) {
+        if (few_ctas)
+            return is_signed ? dispatch_zp<1, true, 1>(zp, fb8, maps, p, smem, stream)
+                             : dispatch_zp<1, false, 1>(zp, fb8, maps, p, smem, stream);
+        return is_signed ? dispatch_zp<1, true, 2>(zp, fb8, maps, p, smem, stream)
+                         : dispatch_zp<1, false, 2>(zp, fb8, maps, p, smem, stream);
+    }
+    return is_signed ? dispatch_zp<2, true, 2>(zp, fb8, maps, p, smem, stream)
+                     : dispatch_zp<2, false, 2>(zp, fb8, maps, p, smem, stream);
 }
 
 // Shared memory an SM offers two co-resident CTAs, and one CTA alone.
@@ -665,7 +675,7 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
         maps.z_wide = maps.s_wide;       // never read
         maps.z_narrow = maps.s_narrow;
     }
-    return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, maps, p, smem, stream);
+    return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, 2 * p.G <= sm_count(), maps, p, smem, stream);
 }
 
 }  // namespace t4b

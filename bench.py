@@ -187,6 +187,75 @@ def prefill_gemm(dev, M=4096, steps=5, warmup=3):
             "per_shape": per_shape}
 
 
+def _graph_us(dev, calls, reps=20):
+    """Average device time of one call in a CUDA graph of `calls` (a list of
+    zero-argument callables, replayed `reps` times after warm-up)."""
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for f in calls:
+            f()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in calls:
+            f()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * len(calls))
+    del g
+    return us
+
+
+def int3_and_dequant(dev):
+    """The other hot-path kernels at BASELINE-config shapes, device time per
+    launch in a graph, inputs rotating through >= 4x L2:
+      * H17 INT3 GEMV, M = 1, K in {4100, 14340} (4096 / 14336 padded to a
+        multiple of 10), N in {4096, 14336}, group 128, no zero points; bytes
+        = (K/10) N 4 + ceil(K/128) N 2 + 2 K + 2 N;
+      * flat dequantization (s4 and s3 magic, fp8) of a 4096 x 14336 weight's
+        words with per-word scales / zero points; bytes = read + written."""
+    from t4_cuda_b200 import ops
+    gen = torch.Generator(device=dev).manual_seed(9)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    out = {"int3_gemv": {}, "dequant": {}}
+    for K, N in ((4100, 4096), (4100, 14336), (14340, 4096), (14340, 14336)):
+        G = -(-K // 128)
+        wbytes = (K // 10) * N * 4
+        pool = max(4, (4 * l2) // wbytes + 1)
+        Ws = [torch.randint(0, 2 ** 30, (K // 10, N), dtype=torch.int32, device=dev, generator=gen) for _ in range(pool)]
+        S = (torch.randn((G, N), device=dev, generator=gen).abs() * 0.02).half()
+        A = torch.randn((1, K), device=dev, generator=gen).half()
+        Z = torch.empty(0, dtype=torch.float16, device=dev)
+        us = _graph_us(dev, [lambda W=W: ops.fused_h17_gemv_s3(A, W, S, Z, group_size=128) for W in Ws])
+        alg = wbytes + G * N * 2 + K * 2 + N * 2
+        out["int3_gemv"][f"{K}x{N}"] = {"us": round(us, 3), "GB/s": round(alg / us / 1e3, 1)}
+        del Ws
+    words = 4096 // 8 * 14336
+    for kind, per_word, fn in (("s4", 8, ops.dequantize_s4), ("s3", 10, ops.dequantize_s3), ("fp8", 4, None)):
+        pool = max(4, (4 * l2) // (words * (4 + 4 + 2 * per_word)) + 1)
+        Ws = [torch.randint(0, 2 ** 30, (words,), dtype=torch.int32, device=dev, generator=gen) for _ in range(pool)]
+        S = (torch.randn(words, device=dev, generator=gen) * 0.02).half()
+        Zp = torch.zeros(words, device=dev, dtype=torch.float16)
+        if kind == "fp8":
+            calls = [lambda W=W: ops.dequantize_fp8(W, S, mode="magic") for W in Ws]
+            byts = words * (4 + 2 + 2 * per_word)
+        else:
+            calls = [lambda W=W, fn=fn: fn(W, S, Zp, mode="magic") for W in Ws]
+            byts = words * (4 + 2 + 2 + 2 * per_word)
+        us = _graph_us(dev, calls)
+        out["dequant"][kind] = {"words": words, "us": round(us, 3), "GB/s": round(byts / us / 1e3, 1)}
+        del Ws
+    return out
+
+
 def run_ours(args):
     from t4_cuda_b200 import ops
     from t4_cuda_b200.shard import ShardedGroup, ShardedLinear
@@ -292,6 +361,9 @@ def run_ours(args):
     gemm = None
     if world == 1 and not args.no_gemm:
         gemm = prefill_gemm(dev)
+    others = None
+    if world == 1 and not args.no_gemm:
+        others = int3_and_dequant(dev)
 
     # ---- end to end through the public API, host buffers, copies timed
     pin = {a: t.cpu().pin_memory() for a, t in acts.items()}
@@ -374,6 +446,8 @@ def run_ours(args):
                             "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)" if peaks["source"] == "measured"
                             else "fallback 1590 TFLOP/s", "traffic": None}
         line["gemm"] = gemm
+    if others is not None:
+        line["other_kernels"] = others
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
     print(json.dumps(line), flush=True)

@@ -356,7 +356,10 @@ int fused_int3(const void* A, const void* W, const void* S, const void* Z, void*
     const int mt = (M <= 8) ? 1 : 2;
     const int tiles = (N + kTileN - 1) / kTileN;
     const int chunks = (M + 8 * mt - 1) / (8 * mt);
-    int splits = (2 * sm_count() + tiles * chunks - 1) / (tiles * chunks);
+    // One CTA per SM fits (the kernel holds ~140 registers per thread), so
+    // split K only as far as one wave of CTAs covers the SMs: a second wave
+    // would repeat the whole load round trip.
+    int splits = sm_count() / (tiles * chunks);
     if (splits > 8) splits = 8;
     while (splits > 1 && splits * kWarps > p.total_steps) --splits;
     if (splits < 1) splits = 1;

@@ -64,7 +64,8 @@ struct Shape {
     static constexpr int kThreads = 32 * (kWarps + 1);         // + one producer warp
     static constexpr int kWeightBytes = kWarps * 2048;         // packed words per stage
     static constexpr int kRowsNarrow = 16 * kWarps;            // stage rows, 1 warp column (1-2 tiles)
-    static constexpr int kRowsWide = 8 * kWarps;               // stage rows, 2 warp columns (3-4 tiles)
+    static constexpr int kRowsWide = 8 * kWarps;               // stage rows, 2 warp columns (4 tiles)
+    static constexpr int kRowsSplit = 32 * kWarps;             // stage rows of a split group (1 tile, two row halves)
 };
 
 // Device error word of this kernel (bit 0: a bounded wait gave up), one per
@@ -87,7 +88,10 @@ struct DecodeParams {
     int stages;         // ring depth
     int early;          // stages issued before griddepcontrol.wait (the rest right after it)
     int slot_bytes;     // bytes of one ring slot
-    int s_wide, s_narrow;   // stages of a tile group with 2 / 1 warp columns
+    int s_wide, s_narrow;   // stages of a wide (4-tile) / narrow (1-2 tile) group
+    int split;          // a lone tile streams as a split group (M <= 4; see cta_plan)
+    int s_split;        // stages of a split group
+    int sbr_split;      // scale rows of a split stage's scale box
     int act_bytes;      // resident activation records (bytes)
     int sum_floats;     // flush-block activation sums
     int red_floats;     // cross-warp reduction buffer
@@ -101,6 +105,8 @@ struct DecodeMaps {
     CUtensorMap s_narrow;   // scales, box 32 columns x sbr_narrow rows
     CUtensorMap z_wide;     // zero points, same boxes (unused without them)
     CUtensorMap z_narrow;
+    CUtensorMap s_split;    // scales, box 16 columns x sbr_split rows
+    CUtensorMap z_split;
 };
 
 // A pure function of its operands (not volatile), so the compiler may
@@ -130,6 +136,12 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     return v;
 }
 
+__device__ __forceinline__ float lds32f(uint32_t addr) {
+    float v;
+    asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
     uint2 v;
     asm("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
@@ -155,9 +167,26 @@ __device__ __forceinline__ void unpack_offset64(uint32_t w, uint32_t (&e)[4]) {
 __device__ __forceinline__ int row_of(int j, int c) { return (c & 1) + 4 * (c >> 1) + 2 * (j & 1) + 8 * (j >> 1); }
 
 struct CtaPlan {
-    int t0, ng, nt_last, s_last, total;
+    int t0;         // first tile
+    int n4;         // groups of four tiles (wide)
+    int rem;        // tiles after them (0..3): 2 or 3 -> one narrow group of 2; odd -> one lone tile
+    int ng, total;  // groups, stages
 };
 
+// A CTA's n tiles are groups of four ("wide": 2 warp columns of 32 columns,
+// rows_wide rows per stage), then for a remainder of 2 or 3 one "narrow" group
+// of two (1 warp column, rows_narrow rows), then for an odd remainder one lone
+// tile.  For M <= 4 a lone tile is a "split" group: the lanes that would read
+// the second box of a narrow group read the second row half of the same tile
+// instead, so a stage covers rows_split = 2 rows_narrow rows and no lane
+// idles.  An MMA has one K range for all its rows, so the halves are kept
+// apart in the batch dimension: B column n = 2 m + h carries batch row m over
+// row half h (h = n & 1 = bb of the lane that supplies it), and MMA row r --
+// weights of half bb(r) -- keeps only the products with columns of its own
+// half, elements (e & 1) == bb.  Every kind then moves the same
+// 512-word-per-warp stage, so a CTA's stage count is proportional to its tiles
+// (a wide group of 3 tiles idled a quarter of the lanes, a lone narrow tile
+// half of them).  For M > 4 a lone tile is a narrow group of one.
 template <int MT>
 __device__ __forceinline__ CtaPlan cta_plan(const DecodeParams& p) {
     CtaPlan q;
@@ -165,11 +194,39 @@ __device__ __forceinline__ CtaPlan cta_plan(const DecodeParams& p) {
     q.t0 = (int)(b * (uint32_t)p.T / (uint32_t)p.G);          // b * T < 2^32 (checked on the host)
     const int t1 = (int)((b + 1) * (uint32_t)p.T / (uint32_t)p.G);
     const int n = t1 - q.t0;
-    q.ng = (n + 3) >> 2;
-    q.nt_last = n - 4 * (q.ng - 1);
-    q.s_last = (q.nt_last > 2) ? p.s_wide : p.s_narrow;
-    q.total = (q.ng - 1) * p.s_wide + q.s_last;
+    q.n4 = n >> 2;
+    q.rem = n & 3;
+    q.ng = q.n4 + (q.rem >= 2 ? 1 : 0) + (q.rem & 1);
+    q.total = q.n4 * p.s_wide + (q.rem >= 2 ? p.s_narrow : 0) + ((q.rem & 1) ? (p.split ? p.s_split : p.s_narrow) : 0);
     return q;
+}
+
+enum GroupKind { kWide = 0, kNarrow = 1, kSplit = 2 };
+
+struct GroupInfo {
+    int kind, nt, tile0, nst, stage0;
+};
+
+__device__ __forceinline__ GroupInfo group_info(const DecodeParams& p, const CtaPlan& q, int g) {
+    GroupInfo gi;
+    if (g < q.n4) {
+        gi.kind = kWide; gi.nt = 4; gi.tile0 = q.t0 + 4 * g; gi.nst = p.s_wide; gi.stage0 = g * p.s_wide;
+        return gi;
+    }
+    gi.tile0 = q.t0 + 4 * q.n4;
+    gi.stage0 = q.n4 * p.s_wide;
+    if (q.rem >= 2 && g == q.n4) {
+        gi.kind = kNarrow; gi.nt = 2; gi.nst = p.s_narrow;
+        return gi;
+    }
+    if (q.rem >= 2) {           // the lone tile after a narrow group
+        gi.tile0 += 2;
+        gi.stage0 += p.s_narrow;
+    }
+    gi.nt = 1;
+    gi.kind = p.split ? kSplit : kNarrow;
+    gi.nst = p.split ? p.s_split : p.s_narrow;
+    return gi;
 }
 
 // Issue ring stage i (global stage index within this CTA) into `slot`.
@@ -177,34 +234,43 @@ template <int MT, bool HAS_ZP>
 __device__ __forceinline__ void issue_stage(const DecodeParams& p, const CtaPlan& q, const DecodeMaps& maps,
                                             uint8_t* ring, uint64_t* full, int i, int slot) {
     using S = Shape<MT>;
-    const int full_stages = (q.ng - 1) * p.s_wide;
-    int g, ks;
-    if (i < full_stages) {
-        g = i / p.s_wide;
-        ks = i - g * p.s_wide;
-    } else {
-        g = q.ng - 1;
-        ks = i - full_stages;
+    int g = (i < q.n4 * p.s_wide) ? i / p.s_wide : q.n4;
+    GroupInfo gi = group_info(p, q, g);
+    if (i >= gi.stage0 + gi.nst) gi = group_info(p, q, ++g);     // past the narrow group: the lone tile
+    const int ks = i - gi.stage0;
+    uint8_t* base = ring + (size_t)slot * p.slot_bytes;
+    uint8_t* sbase = base + S::kWeightBytes;
+    if (gi.kind == kSplit) {
+        // two boxes of rows_narrow rows: the two row halves of one tile
+        const int row0 = ks * S::kRowsSplit;
+        const uint32_t sbox = (uint32_t)p.sbr_split * 32;
+        mbar_arrive_expect_tx(&full[slot], (uint32_t)(2 * S::kRowsNarrow * 64) + sbox * (HAS_ZP ? 2 : 1));
+        tma_load_2d(base, &maps.w_narrow, kBoxCols * gi.tile0, row0, &full[slot]);
+        tma_load_2d(base + S::kRowsNarrow * 64, &maps.w_narrow, kBoxCols * gi.tile0, row0 + S::kRowsNarrow, &full[slot]);
+        const int sr = (p.gw_shift >= 0) ? (row0 >> p.gw_shift) : row0 / p.gw;
+        tma_load_2d(sbase, &maps.s_split, kBoxCols * gi.tile0, sr, &full[slot]);
+        if constexpr (HAS_ZP) tma_load_2d(sbase + p.s_bytes, &maps.z_split, kBoxCols * gi.tile0, sr, &full[slot]);
+        return;
     }
-    const int nt = (g < q.ng - 1) ? 4 : q.nt_last;
-    const bool wide = nt > 2;
+    const bool wide = gi.kind == kWide;
     const int rows = wide ? S::kRowsWide : S::kRowsNarrow;
     const int row0 = ks * rows;
-    const int tg0 = q.t0 + 4 * g;
     const uint32_t sbox = wide ? (uint32_t)p.sbr_wide * 128 : (uint32_t)p.sbr_narrow * 64;
-    mbar_arrive_expect_tx(&full[slot], (uint32_t)(nt * rows * 64) + sbox * (HAS_ZP ? 2 : 1));
-    uint8_t* base = ring + (size_t)slot * p.slot_bytes;
+    mbar_arrive_expect_tx(&full[slot], (uint32_t)(gi.nt * rows * 64) + sbox * (HAS_ZP ? 2 : 1));
     const CUtensorMap* tw = wide ? &maps.w_wide : &maps.w_narrow;
-    for (int bx = 0; bx < nt; ++bx) tma_load_2d(base + bx * rows * 64, tw, kBoxCols * (tg0 + bx), row0, &full[slot]);
+    for (int bx = 0; bx < gi.nt; ++bx)
+        tma_load_2d(base + bx * rows * 64, tw, kBoxCols * (gi.tile0 + bx), row0, &full[slot]);
     const int sr = (p.gw_shift >= 0) ? (row0 >> p.gw_shift) : row0 / p.gw;
-    uint8_t* sbase = base + S::kWeightBytes;
-    tma_load_2d(sbase, wide ? &maps.s_wide : &maps.s_narrow, kBoxCols * tg0, sr, &full[slot]);
-    if constexpr (HAS_ZP) tma_load_2d(sbase + p.s_bytes, wide ? &maps.z_wide : &maps.z_narrow, kBoxCols * tg0, sr, &full[slot]);
+    tma_load_2d(sbase, wide ? &maps.s_wide : &maps.s_narrow, kBoxCols * gi.tile0, sr, &full[slot]);
+    if constexpr (HAS_ZP)
+        tma_load_2d(sbase + p.s_bytes, wide ? &maps.z_wide : &maps.z_narrow, kBoxCols * gi.tile0, sr, &full[slot]);
 }
 
 // acc += s * (dg + o * sum a) for the two 16-column sub-tiles of this lane,
-// o = -(offset + z).  s / z: the lane's four columns 4L..4L+3.
-template <int MT, bool SIGNED, bool HAS_ZP>
+// o = -(offset + z).  s / z: the lane's four columns 4L..4L+3.  The sums are
+// those of the lane's batch rows 2c, 2c+1 -- or, in a split group (SPLIT), of
+// its one batch row c over its row half, the same value for both.
+template <int MT, bool SIGNED, bool HAS_ZP, bool SPLIT>
 __device__ __forceinline__ void flush(float (&acc)[MT][2][4], const float (&dg)[MT][2][4], uint32_t saddr,
                                       uint32_t zaddr, uint32_t sum_addr) {
     constexpr float kOff = SIGNED ? 72.f : 64.f;
@@ -221,8 +287,14 @@ __device__ __forceinline__ void flush(float (&acc)[MT][2][4], const float (&dg)[
     }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-        const uint2 sv2 = lds64(sum_addr + 32 * mt);
-        const float sa[2] = {__uint_as_float(sv2.x), __uint_as_float(sv2.y)};
+        float sa[2];
+        if constexpr (SPLIT) {
+            sa[0] = sa[1] = lds32f(sum_addr + 32 * mt);
+        } else {
+            const uint2 sv2 = lds64(sum_addr + 32 * mt);
+            sa[0] = __uint_as_float(sv2.x);
+            sa[1] = __uint_as_float(sv2.y);
+        }
 #pragma unroll
         for (int X = 0; X < 2; ++X)
 #pragma unroll
@@ -231,6 +303,192 @@ __device__ __forceinline__ void flush(float (&acc)[MT][2][4], const float (&dg)[
                 acc[mt][X][e] = fmaf(s[k], fmaf(o[k], sa[e & 1], dg[mt][X][e]), acc[mt][X][e]);
             }
     }
+}
+
+// State the math warps carry from one tile group to the next.
+struct MathCtx {
+    uint32_t ring_a, act_a, sums_a, pitch16;
+    float* red;
+    uint64_t* full;
+    uint64_t* empty;
+    volatile int* sflag;
+    int warp, lane, r, c, bb, L;
+    int slot;
+    uint32_t phase;
+    bool aborted;
+};
+
+// This lane's shared-memory offsets in a stage of a KIND group.  Loads are
+// unconditional (a guard around inline asm becomes a branch that splits the
+// stage into small scheduling regions): a lane whose box lies past the
+// group's last tile reads another box of the slot, and a lane past the last
+// batch row reads row M-1; both only feed MMA rows / columns never stored.
+template <int MT>
+struct LaneOffsets {
+    uint32_t woff[4];       // packed words, row step j
+    uint32_t aoff[MT][4];   // activation records, row step j (plus the stage's row0 * 16)
+    uint32_t soff[2];       // scales of flush half h
+    int lane_row;           // first word row of this lane's rows in a stage
+};
+
+template <int MT, int KIND>
+__device__ __forceinline__ LaneOffsets<MT> setup_lane(const DecodeParams& p, const MathCtx& x) {
+    using S = Shape<MT>;
+    constexpr int nwc = (KIND == kWide) ? 2 : 1;                 // warp columns (32 columns each)
+    constexpr int rbs = S::kWarps / nwc;                          // 16-row blocks per box
+    constexpr int box_rows = (KIND == kWide) ? S::kRowsWide : S::kRowsNarrow;
+    constexpr int rows = (KIND == kSplit) ? S::kRowsSplit : box_rows;
+    constexpr int srow_bytes = (KIND == kWide) ? 128 : (KIND == kNarrow ? 64 : 32);
+    LaneOffsets<MT> lo;
+    const int wc = (nwc == 2) ? x.warp / rbs : 0;
+    const int rb = x.warp - wc * rbs;
+    const int box = 2 * wc + x.bb;                                // a split group's box bb is row half bb
+    lo.lane_row = 16 * rb + ((KIND == kSplit) ? x.bb * S::kRowsNarrow : 0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int row = 16 * rb + row_of(j, x.c);                 // row within the box
+        lo.woff[j] = (uint32_t)(box * box_rows * 64 + row * 64) + (uint32_t)((x.L ^ ((row >> 1) & 3)) << 4);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            const int m = (KIND == kSplit) ? min(x.r >> 1, p.M - 1) : min(x.r + 8 * mt, p.M - 1);
+            lo.aoff[mt][j] = x.act_a + (uint32_t)m * x.pitch16 + (uint32_t)(lo.lane_row + row_of(j, x.c)) * 16;
+        }
+    }
+    // scale row of this lane's flush blocks (rows lane_row + 8h of the stage); a
+    // scale box row holds the group's 64 (wide), 32 (narrow) or 16 (split) columns
+    const int scol = (KIND == kSplit) ? 4 * x.L : 16 * box + 4 * x.L;
+    const bool per_row = p.gw_shift >= 0 && p.gw < rows;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int srow = per_row ? ((lo.lane_row + 8 * h) >> p.gw_shift) : 0;
+        lo.soff[h] = (uint32_t)(S::kWeightBytes + srow * srow_bytes + scol * 2);
+    }
+    return lo;
+}
+
+template <int MT>
+__device__ __forceinline__ LaneOffsets<MT> setup_any(int kind, const DecodeParams& p, const MathCtx& x) {
+    if (kind == kWide) return setup_lane<MT, kWide>(p, x);
+    if (MT == 1 && kind == kSplit) return setup_lane<MT, kSplit>(p, x);
+    return setup_lane<MT, kNarrow>(p, x);
+}
+
+// Stream one tile group's stages through the ring and store its outputs.
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int KIND>
+__device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo& gi, const LaneOffsets<MT>& lo,
+                                          MathCtx& x) {
+    using S = Shape<MT>;
+    constexpr int kWarps = S::kWarps;
+    constexpr int kMathThreads = 32 * kWarps;
+    constexpr int nwc = (KIND == kWide) ? 2 : 1;
+    constexpr int rbs = kWarps / nwc;
+    constexpr int rows = (KIND == kSplit) ? S::kRowsSplit : ((KIND == kWide) ? S::kRowsWide : S::kRowsNarrow);
+    constexpr bool kSplitGroup = KIND == kSplit;
+    const uint32_t zdelta = (uint32_t)p.s_bytes;
+    const uint32_t sum_base = kSplitGroup ? x.sums_a + (uint32_t)x.c * 4 : x.sums_a + (uint32_t)(2 * x.c) * 4;
+
+    float acc[MT][2][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int X = 0; X < 2; ++X)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][X][e] = 0.f;
+
+    for (int ks = 0; ks < gi.nst; ++ks) {
+        if (!x.aborted && !mbar_wait_bounded(&x.full[x.slot], x.phase, kWaitLimitNs)) {
+            x.aborted = true;
+            x.sflag[0] = 1;
+            atomicOr(&g_decode_error, kErrTimeout);
+        }
+        if (!x.aborted) {
+            const uint32_t st = x.ring_a + (uint32_t)x.slot * p.slot_bytes;
+            const int row0 = ks * rows;
+            const uint32_t arow = (uint32_t)row0 * 16;
+            float dg[MT][2][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint4 wv = lds128(st + lo.woff[j]);
+                uint4 av[MT];
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) av[mt] = lds128(lo.aoff[mt][j] + arow);
+                uint32_t e0[4], e1[4], e2[4], e3[4];
+                unpack_offset64<SIGNED>(wv.x, e0);   // column 4L     (sub-tile 0, MMA row r)
+                unpack_offset64<SIGNED>(wv.y, e1);   // column 4L + 1 (sub-tile 0, MMA row r + 8)
+                unpack_offset64<SIGNED>(wv.z, e2);   // column 4L + 2 (sub-tile 1, MMA row r)
+                unpack_offset64<SIGNED>(wv.w, e3);   // column 4L + 3 (sub-tile 1, MMA row r + 8)
+                const bool first = (j == 0) || (j == 2 && FB8);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    if (first) {
+                        mma_16816_zero(dg[mt][0], e0[0], e1[0], e0[1], e1[1], av[mt].x, av[mt].y);
+                        mma_16816_zero(dg[mt][1], e2[0], e3[0], e2[1], e3[1], av[mt].x, av[mt].y);
+                    } else {
+                        mma_16816(dg[mt][0], e0[0], e1[0], e0[1], e1[1], av[mt].x, av[mt].y);
+                        mma_16816(dg[mt][1], e2[0], e3[0], e2[1], e3[1], av[mt].x, av[mt].y);
+                    }
+                    mma_16816(dg[mt][0], e0[2], e1[2], e0[3], e1[3], av[mt].z, av[mt].w);
+                    mma_16816(dg[mt][1], e2[2], e3[2], e2[3], e3[3], av[mt].z, av[mt].w);
+                }
+                if (j == 1 && FB8) {
+                    const uint32_t b8 = (uint32_t)((row0 + lo.lane_row) >> 3);
+                    flush<MT, SIGNED, HAS_ZP, kSplitGroup>(acc, dg, st + lo.soff[0], st + lo.soff[0] + zdelta,
+                                                           sum_base + b8 * (32 * MT));
+                }
+            }
+            if (FB8) {
+                const uint32_t b8 = (uint32_t)((row0 + lo.lane_row) >> 3) + 1;
+                flush<MT, SIGNED, HAS_ZP, kSplitGroup>(acc, dg, st + lo.soff[1], st + lo.soff[1] + zdelta,
+                                                       sum_base + b8 * (32 * MT));
+            } else {
+                const uint32_t b16 = (uint32_t)((row0 + lo.lane_row) >> 4);
+                flush<MT, SIGNED, HAS_ZP, kSplitGroup>(acc, dg, st + lo.soff[0], st + lo.soff[0] + zdelta,
+                                                       sum_base + b16 * (32 * MT));
+            }
+        }
+        // Every lane's reads of this slot are complete (their results fed the
+        // MMAs above): release it to the producer.
+        __syncwarp();
+        if (x.lane == 0) mbar_arrive(&x.empty[x.slot]);
+        if (++x.slot == p.stages) {
+            x.slot = 0;
+            x.phase ^= 1u;
+        }
+    }
+
+    // ---- group done: sum the row blocks of each warp column in a fixed order
+    const int M = p.M;
+    float* red = x.red;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int X = 0; X < 2; ++X)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int col = 16 * x.bb + 4 * x.L + 2 * X + (e >> 1);
+                if (kSplitGroup) {       // batch row c, own row half only
+                    if ((e & 1) == x.bb && x.c < M) red[(x.warp * 32 + col) * M + x.c] = acc[mt][X][e];
+                } else {
+                    const int m = 8 * mt + 2 * x.c + (e & 1);
+                    if (m < M) red[(x.warp * 32 + col) * M + m] = acc[mt][X][e];
+                }
+            }
+    named_barrier(1, kMathThreads);
+    const int col_base = kBoxCols * gi.tile0;
+    int ncols = kBoxCols * gi.nt;
+    if (col_base + ncols > p.N) ncols = p.N - col_base;
+    for (int pair = x.warp; pair < nwc * M; pair += kWarps) {
+        const int w = pair / M, m = pair - w * M;
+        const int col = 32 * w + x.lane;
+        if (col < ncols) {
+            float v = 0.f;
+            for (int k = 0; k < rbs; ++k) v += red[((w * rbs + k) * 32 + x.lane) * M + m];
+            if (kSplitGroup)     // the second row half sits in columns 16..31 of each row block
+                for (int k = 0; k < rbs; ++k) v += red[(k * 32 + x.lane + kBoxCols) * M + m];
+            p.C[(size_t)m * p.N + col_base + col] = __half_as_ushort(__float2half_rn(v));
+        }
+    }
+    named_barrier(1, kMathThreads);
 }
 
 // MINB: CTAs per SM the register budget is sized for.  2 leaves room for the
@@ -278,9 +536,11 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
             prefetch_tmap(&maps.w_narrow);
             prefetch_tmap(&maps.s_wide);
             prefetch_tmap(&maps.s_narrow);
+            prefetch_tmap(&maps.s_split);
             if constexpr (HAS_ZP) {
                 prefetch_tmap(&maps.z_wide);
                 prefetch_tmap(&maps.z_narrow);
+                prefetch_tmap(&maps.z_split);
             }
             // weights, scales and zero points are never written by a kernel of
             // this library, so they may be fetched before the previous kernel ends
@@ -309,62 +569,26 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     // ---- per-lane constants and the offsets of the first tile group: none of
     // it depends on the previous kernel, so the math warps compute it while
     // that kernel drains instead of after the activations are in.
-    const int warp = tid >> 5, lane = tid & 31;
-    const int r = lane >> 2, c = lane & 3;
-    const int bb = r & 1;                     // which of the warp's two boxes
-    const int L = (r >> 1) ^ (r & 1);         // 16-byte chunk (4 columns) of that box
-    const uint32_t ring_a = smem_addr(ring);
-    const uint32_t act_a = smem_addr(act);
-    const uint32_t sum_lane = smem_addr(sums) + (uint32_t)(2 * c) * 4;
-    const uint32_t pitch16 = (uint32_t)(p.KWp + 2) * 16;
-    constexpr bool fb8 = FB8;     // 8-row flush blocks (group 64), else 16
-
-    // Offsets of tile group g for this lane.  Loads are unconditional (a guard
-    // around inline asm becomes a branch that splits the stage into small
-    // scheduling regions): a lane whose box lies past the group's last tile
-    // reads another box of the slot, and a lane past the last batch row reads
-    // row M-1; both only feed MMA rows / columns that are never stored.
-    int nt, nwc, rbs, rows, nst, kw_lane;
-    uint32_t woff[4], aoff[MT][4], soff[2];
-    auto setup_group = [&](int g) {
-        nt = (g < q.ng - 1) ? 4 : q.nt_last;
-        nwc = (nt + 1) >> 1;                      // warp columns (32 columns each)
-        rbs = kWarps / nwc;                       // 16-row blocks per stage
-        rows = 16 * rbs;
-        nst = (nwc == 2) ? p.s_wide : p.s_narrow;
-        const int wc = (nwc == 2) ? warp / (kWarps / 2) : 0;
-        const int rb = warp - wc * rbs;           // 16-row block of the stage
-        const int box = 2 * wc + bb;
-        kw_lane = 16 * rb;                        // first word row of this warp in a stage
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int row = kw_lane + row_of(j, c);
-            woff[j] = (uint32_t)(box * rows * 64 + row * 64) + (uint32_t)((L ^ ((row >> 1) & 3)) << 4);
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                const int m = min(r + 8 * mt, p.M - 1);
-                aoff[mt][j] = act_a + (uint32_t)m * pitch16 + (uint32_t)row * 16;
-            }
-        }
-        // scale row of this warp's flush blocks (rows kw_lane + 8h of the stage);
-        // a scale box row holds the group's 64 (wide) or 32 (narrow) columns
-        const int srow_bytes = (nwc == 2) ? 128 : 64;
-        const bool per_row = p.gw_shift >= 0 && p.gw < rows;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int srow = per_row ? ((kw_lane + 8 * h) >> p.gw_shift) : 0;
-            soff[h] = (uint32_t)(S::kWeightBytes + srow * srow_bytes + (16 * box + 4 * L) * 2);
-        }
-    };
-    setup_group(0);
-
-    float acc[MT][2][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int X = 0; X < 2; ++X)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[mt][X][e] = 0.f;
+    MathCtx x;
+    x.warp = tid >> 5;
+    x.lane = tid & 31;
+    x.r = x.lane >> 2;
+    x.c = x.lane & 3;
+    x.bb = x.r & 1;                           // which of the warp's two boxes (row half in a split group)
+    x.L = (x.r >> 1) ^ (x.r & 1);             // 16-byte chunk (4 columns) of that box
+    x.ring_a = smem_addr(ring);
+    x.act_a = smem_addr(act);
+    x.sums_a = smem_addr(sums);
+    x.pitch16 = (uint32_t)(p.KWp + 2) * 16;
+    x.red = red;
+    x.full = full;
+    x.empty = empty;
+    x.sflag = sflag;
+    x.slot = 0;
+    x.phase = 0;
+    x.aborted = false;
+    GroupInfo gi = group_info(p, q, 0);
+    LaneOffsets<MT> lo = setup_any<MT>(gi.kind, p, x);
 
     pdl_wait_prior_grid();     // A and C may belong to the previous kernel
 
@@ -417,101 +641,18 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     named_barrier(1, kMathThreads);
     if (tid == 0) mbar_arrive(prep_done);
 
-    bool aborted = false;
-    int i = 0, slot = 0;
-    uint32_t phase = 0;
     for (int g = 0; g < q.ng; ++g) {
-        if (g > 0) setup_group(g);
-        const uint32_t zdelta = (uint32_t)p.s_bytes;
-
-        for (int ks = 0; ks < nst; ++ks, ++i) {
-            if (!aborted && !mbar_wait_bounded(&full[slot], phase, kWaitLimitNs)) {
-                aborted = true;
-                sflag[0] = 1;
-                atomicOr(&g_decode_error, kErrTimeout);
-            }
-            if (!aborted) {
-                const uint32_t st = ring_a + (uint32_t)slot * p.slot_bytes;
-                const int row0 = ks * rows;
-                const uint32_t arow = (uint32_t)row0 * 16;
-                float dg[MT][2][4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint4 wv = lds128(st + woff[j]);
-                    uint4 av[MT];
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) av[mt] = lds128(aoff[mt][j] + arow);
-                    uint32_t e0[4], e1[4], e2[4], e3[4];
-                    unpack_offset64<SIGNED>(wv.x, e0);   // column 4L     (sub-tile 0, MMA row r)
-                    unpack_offset64<SIGNED>(wv.y, e1);   // column 4L + 1 (sub-tile 0, MMA row r + 8)
-                    unpack_offset64<SIGNED>(wv.z, e2);   // column 4L + 2 (sub-tile 1, MMA row r)
-                    unpack_offset64<SIGNED>(wv.w, e3);   // column 4L + 3 (sub-tile 1, MMA row r + 8)
-                    const bool first = (j == 0) || (j == 2 && fb8);
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) {
-                        if (first) {
-                            mma_16816_zero(dg[mt][0], e0[0], e1[0], e0[1], e1[1], av[mt].x, av[mt].y);
-                            mma_16816_zero(dg[mt][1], e2[0], e3[0], e2[1], e3[1], av[mt].x, av[mt].y);
-                        } else {
-                            mma_16816(dg[mt][0], e0[0], e1[0], e0[1], e1[1], av[mt].x, av[mt].y);
-                            mma_16816(dg[mt][1], e2[0], e3[0], e2[1], e3[1], av[mt].x, av[mt].y);
-                        }
-                        mma_16816(dg[mt][0], e0[2], e1[2], e0[3], e1[3], av[mt].z, av[mt].w);
-                        mma_16816(dg[mt][1], e2[2], e3[2], e2[3], e3[3], av[mt].z, av[mt].w);
-                    }
-                    if (j == 1 && fb8) {
-                        const uint32_t b8 = (uint32_t)((row0 + kw_lane) >> 3);
-                        flush<MT, SIGNED, HAS_ZP>(acc, dg, st + soff[0], st + soff[0] + zdelta,
-                                                  sum_lane + b8 * (32 * MT));
-                    }
-                }
-                if (fb8) {
-                    const uint32_t b8 = (uint32_t)((row0 + kw_lane) >> 3) + 1;
-                    flush<MT, SIGNED, HAS_ZP>(acc, dg, st + soff[1], st + soff[1] + zdelta,
-                                              sum_lane + b8 * (32 * MT));
-                } else {
-                    const uint32_t b16 = (uint32_t)((row0 + kw_lane) >> 4);
-                    flush<MT, SIGNED, HAS_ZP>(acc, dg, st + soff[0], st + soff[0] + zdelta,
-                                              sum_lane + b16 * (32 * MT));
-                }
-            }
-            // Every lane's reads of this slot are complete (their results fed
-            // the MMAs above): release it to the producer.
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            if (++slot == p.stages) {
-                slot = 0;
-                phase ^= 1u;
-            }
+        if (g > 0) {
+            gi = group_info(p, q, g);
+            lo = setup_any<MT>(gi.kind, p, x);
         }
-
-        // ---- group done: sum the row blocks of each warp column in a fixed order
-        const int M = p.M;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int X = 0; X < 2; ++X)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int col = 16 * bb + 4 * L + 2 * X + (e >> 1);
-                    const int m = 8 * mt + 2 * c + (e & 1);
-                    if (m < M) red[(warp * 32 + col) * M + m] = acc[mt][X][e];
-                    acc[mt][X][e] = 0.f;
-                }
-        named_barrier(1, kMathThreads);
-        const int col_base = kBoxCols * (q.t0 + 4 * g);
-        int ncols = kBoxCols * nt;
-        if (col_base + ncols > p.N) ncols = p.N - col_base;
-        for (int pair = warp; pair < nwc * M; pair += kWarps) {
-            const int w = pair / M, m = pair - w * M;
-            const int col = 32 * w + lane;
-            if (col < ncols) {
-                float v = 0.f;
-                for (int k = 0; k < rbs; ++k) v += red[((w * rbs + k) * 32 + lane) * M + m];
-                p.C[(size_t)m * p.N + col_base + col] = __half_as_ushort(__float2half_rn(v));
-            }
+        if (gi.kind == kWide) {
+            run_group<MT, SIGNED, HAS_ZP, FB8, kWide>(p, gi, lo, x);
+        } else if (MT == 1 && gi.kind == kSplit) {
+            run_group<MT, SIGNED, HAS_ZP, FB8, kSplit>(p, gi, lo, x);
+        } else {
+            run_group<MT, SIGNED, HAS_ZP, FB8, kNarrow>(p, gi, lo, x);
         }
-        named_barrier(1, kMathThreads);
     }
     }   // math warps
 
@@ -607,7 +748,7 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
     if (!aligned(A, 16) || !aligned(W, 16) || !aligned(S, 16) || (Z && !aligned(Z, 16))) return T4B_ERR_UNSUPPORTED;
     const int MT = (M <= 8) ? 1 : 2;
     const int warps = (MT == 1) ? Shape<1>::kWarps : Shape<2>::kWarps;
-    const int rows_narrow = 16 * warps, rows_wide = 8 * warps;
+    const int rows_narrow = 16 * warps, rows_wide = 8 * warps, rows_split = 32 * warps;
     // a flush block (8 or 16 word rows) and a scale box (rows_wide rows) must
     // each lie in one group
     auto box_rows = [&](int rows) { return rows % gw == 0 ? rows / gw : (gw % rows == 0 ? 1 : 0); };
@@ -616,7 +757,9 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
     p.A = static_cast<const uint16_t*>(A);
     p.C = static_cast<uint16_t*>(C);
     p.M = M; p.N = N; p.K = K; p.KW = KW;
-    p.KWp = (KW + rows_narrow - 1) / rows_narrow * rows_narrow;
+    p.split = (box_rows(rows_split) && M <= 4) ? 1 : 0;         // split groups use 2 batch columns per row
+    const int pad_rows = p.split ? rows_split : rows_narrow;       // a split stage may run past KW
+    p.KWp = (KW + pad_rows - 1) / pad_rows * pad_rows;
     p.T = (N + kBoxCols - 1) / kBoxCols;
     p.G = p.T < sm_count() ? p.T : sm_count();
     if ((long long)p.T * p.G >= (1ll << 32)) return T4B_ERR_UNSUPPORTED;
@@ -630,9 +773,11 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
     p.fb = (gw == 8) ? 8 : 16;
     p.sbr_wide = box_rows(rows_wide);
     p.sbr_narrow = box_rows(rows_narrow);
-    p.s_bytes = std::max(p.sbr_wide * 128, p.sbr_narrow * 64);
+    p.sbr_split = p.split ? box_rows(rows_split) : 1;
+    p.s_bytes = std::max(std::max(p.sbr_wide * 128, p.sbr_narrow * 64), p.sbr_split * 32);
     p.s_wide = (KW + rows_wide - 1) / rows_wide;
     p.s_narrow = (KW + rows_narrow - 1) / rows_narrow;
+    p.s_split = (KW + rows_split - 1) / rows_split;
     p.act_bytes = M * (p.KWp + 2) * 16;
     p.sum_floats = (p.KWp / p.fb) * 8 * MT;
     p.red_floats = warps * 32 * M;
@@ -665,15 +810,18 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
     if (!make_tmap_2d_ex(&maps.w_wide, false, W, (uint64_t)KW, (uint64_t)N, rows_wide, kBoxCols, 64, 128) ||
         !make_tmap_2d_ex(&maps.w_narrow, false, W, (uint64_t)KW, (uint64_t)N, rows_narrow, kBoxCols, 64, 128) ||
         !make_tmap_2d_ex(&maps.s_wide, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_wide, 4 * kBoxCols, 0, 0) ||
-        !make_tmap_2d_ex(&maps.s_narrow, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_narrow, 2 * kBoxCols, 0, 0))
+        !make_tmap_2d_ex(&maps.s_narrow, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_narrow, 2 * kBoxCols, 0, 0) ||
+        !make_tmap_2d_ex(&maps.s_split, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_split, kBoxCols, 0, 0))
         return T4B_ERR_UNSUPPORTED;
     if (Z) {
         if (!make_tmap_2d_ex(&maps.z_wide, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_wide, 4 * kBoxCols, 0, 0) ||
-            !make_tmap_2d_ex(&maps.z_narrow, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_narrow, 2 * kBoxCols, 0, 0))
+            !make_tmap_2d_ex(&maps.z_narrow, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_narrow, 2 * kBoxCols, 0, 0) ||
+            !make_tmap_2d_ex(&maps.z_split, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_split, kBoxCols, 0, 0))
             return T4B_ERR_UNSUPPORTED;
     } else {
         maps.z_wide = maps.s_wide;       // never read
         maps.z_narrow = maps.s_narrow;
+        maps.z_split = maps.s_split;
     }
     return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, 2 * p.G <= sm_count(), maps, p, smem, stream);
 }

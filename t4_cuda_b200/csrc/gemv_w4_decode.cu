@@ -305,12 +305,38 @@ __device__ __forceinline__ void flush(float (&acc)[MT][2][4], const float (&dg)[
     }
 }
 
+// Barrier operations by 32-bit shared-memory address (the math warps keep
+// addresses, not 64-bit generic pointers, live across the stage loop).
+__device__ __forceinline__ bool try_wait_a(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool wait_bounded_a(uint32_t bar, uint32_t parity) {
+    if (try_wait_a(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (try_wait_a(bar, parity)) return true;
+        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void arrive_a(uint32_t bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
 // State the math warps carry from one tile group to the next.
 struct MathCtx {
     uint32_t ring_a, act_a, sums_a, pitch16;
+    uint32_t full_a, empty_a;   // barrier arrays (8 bytes per slot)
     float* red;
-    uint64_t* full;
-    uint64_t* empty;
     volatile int* sflag;
     int warp, lane, r, c, bb, L;
     int slot;
@@ -396,7 +422,7 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
             for (int e = 0; e < 4; ++e) acc[mt][X][e] = 0.f;
 
     for (int ks = 0; ks < gi.nst; ++ks) {
-        if (!x.aborted && !mbar_wait_bounded(&x.full[x.slot], x.phase, kWaitLimitNs)) {
+        if (!x.aborted && !wait_bounded_a(x.full_a + 8u * (uint32_t)x.slot, x.phase)) {
             x.aborted = true;
             x.sflag[0] = 1;
             atomicOr(&g_decode_error, kErrTimeout);
@@ -449,7 +475,7 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
         // Every lane's reads of this slot are complete (their results fed the
         // MMAs above): release it to the producer.
         __syncwarp();
-        if (x.lane == 0) mbar_arrive(&x.empty[x.slot]);
+        if (x.lane == 0) arrive_a(x.empty_a + 8u * (uint32_t)x.slot);
         if (++x.slot == p.stages) {
             x.slot = 0;
             x.phase ^= 1u;
@@ -581,8 +607,8 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     x.sums_a = smem_addr(sums);
     x.pitch16 = (uint32_t)(p.KWp + 2) * 16;
     x.red = red;
-    x.full = full;
-    x.empty = empty;
+    x.full_a = smem_addr(full);
+    x.empty_a = smem_addr(empty);
     x.sflag = sflag;
     x.slot = 0;
     x.phase = 0;

@@ -121,8 +121,52 @@ bool make_tmap_f16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
     return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, rows, cols, box_rows, box_cols);
 }
 
+namespace {
+
+// Encoded tensor maps, per host thread, keyed by every encoding parameter.  A
+// decode call encodes six to eight maps, and a model calls the same weights
+// every token: the driver's encode is then the largest host cost of a call.
+// A map depends on nothing but its key (base address, shape, box, swizzle,
+// L2 promotion), so a hit is exactly what a fresh encode would produce.
+struct TmapKey {
+    const void* base;
+    uint64_t rows, cols;
+    uint32_t box_rows, box_cols;
+    int swizzle, l2, fp16;
+    bool operator==(const TmapKey& o) const {
+        return base == o.base && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
+               box_cols == o.box_cols && swizzle == o.swizzle && l2 == o.l2 && fp16 == o.fp16;
+    }
+};
+
+struct TmapEntry {
+    TmapKey key;
+    CUtensorMap map;
+    bool valid;
+};
+
+constexpr int kTmapCacheSize = 512;      // direct-mapped
+thread_local TmapEntry t_tmap_cache[kTmapCacheSize];
+
+uint32_t tmap_hash(const TmapKey& k) {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.base) * 0x9E3779B97F4A7C15ull;
+    h ^= (k.rows * 0xC2B2AE3D27D4EB4Full) + (k.cols << 17) + ((uint64_t)k.box_rows << 40) + ((uint64_t)k.box_cols << 29);
+    h ^= (uint64_t)(k.swizzle * 7 + k.l2 * 131 + k.fp16 * 65537);
+    h ^= h >> 29;
+    return (uint32_t)(h % kTmapCacheSize);
+}
+
+}  // namespace
+
 bool make_tmap_2d_ex(CUtensorMap* map, bool fp16, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
                      uint32_t box_cols, int swizzle_bytes, int l2_promotion_bytes) {
+    const TmapKey key{base, rows, cols, box_rows, box_cols, swizzle_bytes, l2_promotion_bytes, fp16 ? 1 : 0};
+    TmapEntry& slot = t_tmap_cache[tmap_hash(key)];
+    if (slot.valid && slot.key == key) {
+        *map = slot.map;
+        return true;
+    }
+    slot.valid = false;
     auto fn = encode_fn();
     if (!fn) return false;
     const uint32_t esize = fp16 ? 2 : 4;
@@ -142,9 +186,13 @@ bool make_tmap_2d_ex(CUtensorMap* map, bool fp16, const void* base, uint64_t row
     cuuint64_t strides[1] = {cols * esize};
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    return fn(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 2,
-              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, l2,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (fn(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims,
+           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    slot.key = key;
+    slot.map = *map;
+    slot.valid = true;
+    return true;
 }
 
 }  // namespace t4b

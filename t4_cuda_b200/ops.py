@@ -250,8 +250,8 @@ def _fused(name, A, W_packed, scales, zero_points):
     S_ = scales if scales.is_contiguous() else scales.contiguous()
     Z_ = (zero_points if zero_points.is_contiguous() else zero_points.contiguous()) if has_zp else None
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
-    idx = dev.index if dev.index is not None else torch.cuda.current_device()
     cur = torch.cuda.current_device()
+    idx = dev.index if dev.index is not None else cur
     if cur != idx:
         torch.cuda.set_device(idx)
     try:

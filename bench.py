@@ -306,6 +306,12 @@ def run_ours(args):
             token(acts)
         run_step = graph.replay
     else:
+        # each rank's local projections of a gather group replay as one CUDA
+        # graph; the NCCL all-gathers run between them from the host
+        for groups in pg_layers:
+            for g, (a, names) in enumerate(GATHERS):
+                groups[g].capture_local(acts[a])
+
         def run_step():
             token(acts)
 
@@ -401,6 +407,10 @@ def run_ours(args):
 
     if use_graph:
         del graph
+    for groups in pg_layers:
+        for grp in groups.values():
+            grp.release_graph()
+    torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -429,7 +439,8 @@ def run_ours(args):
                    "M": M, "group": GROUP, "layers_per_step": N_LAYERS, "distinct_weight_layers": pool,
                    "weight_pool_bytes": pool * layer_bytes_local, "l2_bytes": l2,
                    "l2_policy": "weights rotate through a pool >= 4x L2 (inputs larger than L2)",
-                   "parallelism": f"column-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "parallelism": (f"column-shard x{world} + NCCL all-gather (local projections of each gather group "
+                                   f"replayed as a CUDA graph, all-gathers from the host)") if world > 1 else "single GPU",
                    "frac_of_8TBs": round(value / 8000.0, 4)},
         "gpu_launches": launches_per_step * args.steps,
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,

@@ -78,19 +78,57 @@ class ShardedGroup:
         self.linears = list(linears)
         self.pg = process_group
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self._graph = None
 
-    def __call__(self, x):
+    def capture_local(self, x):
+        """Record this rank's local projections of activation ``x`` and their
+        packing as one CUDA graph; a later call with the same ``x`` tensor (an
+        activation buffer that stays in place) replays it instead of launching
+        each kernel from Python.  The collective stays outside the graph."""
+        s = torch.cuda.Stream(x.device)
+        s.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._local_packed(x)
+        torch.cuda.current_stream(x.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            packed, widths = self._local_packed(x)
+        self._graph, self._x, self._packed, self._widths = g, x, packed, widths
+
+    def release_graph(self):
+        self._graph = self._x = self._packed = None
+
+    def _local_packed(self, x):
         locals_ = [lin.local(x) for lin in self.linears]
-        if self.world == 1:
-            return locals_
-        M = locals_[0].size(0)
         widths = [t.size(1) for t in locals_]
         packed = torch.cat(locals_, dim=1) if len(locals_) > 1 else locals_[0]
+        return packed, widths
+
+    def __call__(self, x):
+        if self._graph is not None and x is self._x:
+            self._graph.replay()
+            packed, widths = self._packed, self._widths
+        else:
+            if self.world == 1:
+                return [lin.local(x) for lin in self.linears]
+            packed, widths = self._local_packed(x)
+        if self.world == 1:
+            return [t.clone() for t in _split_columns(packed, widths)]
+        M = packed.size(0)
         # gathered flat as [G * M, w] (rank-major), the form every backend
         # accepts for all_gather_into_tensor, then viewed as [G, M, w]
         gathered = torch.empty((self.world * M, packed.size(1)), dtype=packed.dtype, device=packed.device)
         dist.all_gather_into_tensor(gathered, packed.contiguous(), group=self.pg)
         return unpack_gathered(gathered.view(self.world, M, packed.size(1)), widths)
+
+
+def _split_columns(packed, widths):
+    outs, off = [], 0
+    for w in widths:
+        outs.append(packed[:, off:off + w])
+        off += w
+    return outs
 
 
 def unpack_gathered(gathered, widths):

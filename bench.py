@@ -13,8 +13,9 @@ value = algorithmic bytes / second over all ranks, algorithmic bytes per
 projection = K*N/2 + (K/128)*N*2 + M*K*2 + M*N*2.
 
 With --gpus N > 1 (torchrun, one process per GPU) every projection is
-column-sharded N ways and the outputs are gathered with NCCL all-gather
-(t4_cuda_b200.shard): the same token, so "scaling" is "strong".
+column-sharded N ways and the outputs are gathered by the decode kernel itself
+(peer stores over NVLink, t4_cuda_b200.shard.P2PGatherGroup; --nccl-gather
+uses NCCL all-gather instead): the same token, so "scaling" is "strong".
 
 --impl reference times the reference's CPU dequant + matmul path
 (tests/test_fused_gemm_correctness.py:22-36, restated in oracle/cpu_path.py)
@@ -258,7 +259,7 @@ def int3_and_dequant(dev):
 
 def run_ours(args):
     from t4_cuda_b200 import ops
-    from t4_cuda_b200.shard import ShardedGroup, ShardedLinear
+    from t4_cuda_b200.shard import P2PGatherGroup, ShardedGroup, ShardedLinear
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -279,8 +280,25 @@ def run_ours(args):
     pool = min(pool, N_LAYERS)
     layers = [make_layer(rank, world, M, dev, gen) for _ in range(pool)]
     acts = {a: torch.randn((M, k), device=dev, generator=gen).half() for a, k in ACT_K.items()}
-    pg_layers = [{g: ShardedGroup([ShardedLinear(L[n][0], L[n][1], None, "s4") for n in names])
-                  for g, (a, names) in enumerate(GATHERS)} for L in layers]
+    # N > 1: the all-gather is fused into the decode GEMV (peer stores over
+    # NVLink, no collective in the step); if that cannot be set up, each
+    # group's local projections replay as a CUDA graph with NCCL all-gathers
+    # between them from the host
+    gather_mode = "single GPU"
+    pg_layers = None
+    if world > 1 and not args.nccl_gather:
+        try:
+            pg_layers = [{g: P2PGatherGroup([ShardedLinear(L[n][0], L[n][1], None, "s4") for n in names], M)
+                          for g, (a, names) in enumerate(GATHERS)} for L in layers]
+            gather_mode = "fused"
+        except Exception as e:          # noqa: BLE001 -- reported in the JSON line
+            print(f"rank {rank}: fused gather unavailable ({e}); NCCL all-gather", file=sys.stderr)
+            pg_layers = None
+    if pg_layers is None:
+        pg_layers = [{g: ShardedGroup([ShardedLinear(L[n][0], L[n][1], None, "s4") for n in names])
+                      for g, (a, names) in enumerate(GATHERS)} for L in layers]
+        if world > 1:
+            gather_mode = "nccl"
 
     def token(act):
         outs = []
@@ -293,7 +311,7 @@ def run_ours(args):
     step_bytes = N_LAYERS * sum(alg_bytes(M, K, N) for _, K, N in PROJ)
     launches_per_step = N_LAYERS * len(PROJ)
 
-    use_graph = world == 1
+    use_graph = gather_mode in ("single GPU", "fused")
     if use_graph:
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -306,8 +324,8 @@ def run_ours(args):
             token(acts)
         run_step = graph.replay
     else:
-        # each rank's local projections of a gather group replay as one CUDA
-        # graph; the NCCL all-gathers run between them from the host
+        # NCCL path: each rank's local projections of a gather group replay as
+        # one CUDA graph; the all-gathers run between them from the host
         for groups in pg_layers:
             for g, (a, names) in enumerate(GATHERS):
                 groups[g].capture_local(acts[a])
@@ -407,9 +425,15 @@ def run_ours(args):
 
     if use_graph:
         del graph
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()          # no rank still writes into another's gather buffers
     for groups in pg_layers:
         for grp in groups.values():
-            grp.release_graph()
+            if isinstance(grp, P2PGatherGroup):
+                grp.close()
+            else:
+                grp.release_graph()
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
@@ -439,8 +463,11 @@ def run_ours(args):
                    "M": M, "group": GROUP, "layers_per_step": N_LAYERS, "distinct_weight_layers": pool,
                    "weight_pool_bytes": pool * layer_bytes_local, "l2_bytes": l2,
                    "l2_policy": "weights rotate through a pool >= 4x L2 (inputs larger than L2)",
-                   "parallelism": (f"column-shard x{world} + NCCL all-gather (local projections of each gather group "
-                                   f"replayed as a CUDA graph, all-gathers from the host)") if world > 1 else "single GPU",
+                   "parallelism": {"single GPU": "single GPU",
+                                   "fused": f"column-shard x{world}, all-gather fused into the decode GEMV "
+                                            "(peer stores over NVLink, completion flags; whole step one CUDA graph)",
+                                   "nccl": f"column-shard x{world} + NCCL all-gather (local projections of each "
+                                           "gather group replayed as a CUDA graph, all-gathers from the host)"}[gather_mode],
                    "frac_of_8TBs": round(value / 8000.0, 4)},
         "gpu_launches": launches_per_step * args.steps,
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
@@ -572,6 +599,7 @@ def main():
     ap.add_argument("--m", type=int, default=1, help="activation rows (decode batch)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nccl-gather", action="store_true", help="N > 1: NCCL all-gather instead of the fused one")
     ap.add_argument("--case", help="profiling driver: decode:K:N:M or gemm:M:K:N (a few launches, no JSON)")
     ap.add_argument("--launches", type=int, default=6, help="launches for --case")
     args = ap.parse_args()

@@ -18,6 +18,7 @@
 #ifndef T4B200_H
 #define T4B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -139,6 +140,44 @@ int t4b_fused_w4a16_gemm_s4(const void* A, const void* W_packed, const void* sca
 int t4b_fused_w4a16_gemv_noalloc(const void* A, const void* W_packed, const void* scales,
                                  const void* zero_points, void* C, int M, int N, int K,
                                  int group_size, int is_signed, void* stream);
+
+/* ---- column-sharded decode GEMV with a fused all-gather over peer memory ---
+ * No counterpart in the reference (it has no multi-GPU code).  Rank `rank` of
+ * `world` GPUs (one process each) holds columns of a projection; instead of a
+ * GEMV followed by an all-gather collective, the decode kernel stores each of
+ * its output columns straight into every rank's output buffer (device pointers
+ * of peer memory, opened with t4b_ipc_open), and the launch that ends a group
+ * (barrier = 1) waits until every rank's columns have arrived: when it
+ * completes, `out[rank]` holds the whole [M, n_total] output.
+ *   out[g]        rank g's output buffer, row pitch n_total fp16 elements;
+ *                 this rank writes columns col_offset .. col_offset + N - 1
+ *   flags[g]      rank g's arrival flags (world uint32, zero at start)
+ *   local_flags   this rank's flags (== flags[rank])
+ *   counter       this rank's two uint32 (zero at start): CTAs done, epoch
+ * Every rank must make the same sequence of calls on the same buffers.  Waits
+ * are bounded (2 s); a rank that gives up sets the device error word.  Returns
+ * T4B_ERR_UNSUPPORTED (nothing launched) for shapes the decode kernel does not
+ * take; the caller then falls back to its collective. */
+typedef struct {
+    void* out[8];
+    unsigned* flags[8];
+    unsigned* local_flags;
+    unsigned* counter;
+    int world, rank, n_total, col_offset, barrier;
+} T4BGather;
+
+int t4b_fused_w4a16_gemv_allgather(const void* A, const void* W_packed, const void* scales,
+                                   const void* zero_points, int M, int N, int K, int group_size,
+                                   int is_signed, const T4BGather* gather, void* stream);
+
+/* Device memory another process on this node can map: cudaMalloc'd and zeroed
+ * (t4b_ipc_alloc), its 64-byte handle (t4b_ipc_handle), the peer's mapping of
+ * a handle (t4b_ipc_open) and their release. */
+int t4b_ipc_alloc(size_t bytes, void** ptr);
+int t4b_ipc_free(void* ptr);
+int t4b_ipc_handle(void* ptr, void* handle64);
+int t4b_ipc_open(const void* handle64, void** ptr);
+int t4b_ipc_close(void* ptr);
 
 /* ---- H17 fused INT3 GEMV ------------------------------------------------
  * C[M, N] (f16) = A[M, K] (f16) x dequant_s3(W)[K, N], W_packed int32 [K/10, N],

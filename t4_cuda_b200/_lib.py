@@ -24,7 +24,28 @@ SIGNATURES = {
     "t4b_fused_w4a16_gemm_s4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_h17_gemv_s3": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_w4a16_gemv_noalloc": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp],
+    "t4b_fused_w4a16_gemv_allgather": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp],
+    "t4b_ipc_alloc": [ctypes.c_size_t, ctypes.POINTER(_vp)],
+    "t4b_ipc_free": [_vp],
+    "t4b_ipc_handle": [_vp, _vp],
+    "t4b_ipc_open": [_vp, ctypes.POINTER(_vp)],
+    "t4b_ipc_close": [_vp],
 }
+
+
+class T4BGather(ctypes.Structure):
+    """include/t4b200.h T4BGather: peer output buffers and flags of a fused all-gather."""
+    _fields_ = [
+        ("out", _vp * 8),
+        ("flags", _vp * 8),
+        ("local_flags", _vp),
+        ("counter", _vp),
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("n_total", ctypes.c_int),
+        ("col_offset", ctypes.c_int),
+        ("barrier", ctypes.c_int),
+    ]
 
 _lock = threading.Lock()
 _lib = None

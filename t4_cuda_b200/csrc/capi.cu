@@ -1,6 +1,8 @@
 // Library-wide C ABI plumbing: status strings, the per-thread CUDA error
 // record, the cached per-device SM count used to size grids, the per-stream
 // workspace of the streaming GEMV, and TMA tensor-map encoding.
+#include <cstring>
+
 #include "common.cuh"
 #include "tma.cuh"
 #include "workspace.h"
@@ -213,6 +215,42 @@ const char* t4b_status_string(int status) {
 }
 
 int t4b_last_cuda_error(void) { return t4b::g_last_cuda_error; }
+
+int t4b_ipc_alloc(size_t bytes, void** ptr) {
+    if (!ptr || bytes == 0) return T4B_ERR_INVALID_VALUE;
+    *ptr = nullptr;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    return e == cudaSuccess ? T4B_OK : t4b::record_cuda_error(e);
+}
+
+int t4b_ipc_free(void* ptr) {
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? T4B_OK : t4b::record_cuda_error(e);
+}
+
+int t4b_ipc_handle(void* ptr, void* handle64) {
+    if (!ptr || !handle64) return T4B_ERR_NULL_POINTER;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "64-byte IPC handle");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+    if (e != cudaSuccess) return t4b::record_cuda_error(e);
+    memcpy(handle64, &h, sizeof(h));
+    return T4B_OK;
+}
+
+int t4b_ipc_open(const void* handle64, void** ptr) {
+    if (!handle64 || !ptr) return T4B_ERR_NULL_POINTER;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? T4B_OK : t4b::record_cuda_error(e);
+}
+
+int t4b_ipc_close(void* ptr) {
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? T4B_OK : t4b::record_cuda_error(e);
+}
 
 int t4b_version(void) { return (1 << 16) | 1; }
 

@@ -96,6 +96,12 @@ struct DecodeParams {
     int sum_floats;     // flush-block activation sums
     int red_floats;     // cross-warp reduction buffer
     FastDiv kwdiv;      // division by KWp
+    // fused all-gather (world > 1): each output column goes to every rank's buffer
+    uint16_t* peer_out[8];
+    unsigned* peer_flags[8];
+    unsigned* local_flags;
+    unsigned* counter;
+    int world, rank, n_total, col_offset, barrier;
 };
 
 struct DecodeMaps {
@@ -511,10 +517,53 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
             for (int k = 0; k < rbs; ++k) v += red[((w * rbs + k) * 32 + x.lane) * M + m];
             if (kSplitGroup)     // the second row half sits in columns 16..31 of each row block
                 for (int k = 0; k < rbs; ++k) v += red[(k * 32 + x.lane + kBoxCols) * M + m];
-            p.C[(size_t)m * p.N + col_base + col] = __half_as_ushort(__float2half_rn(v));
+            const uint16_t h = __half_as_ushort(__float2half_rn(v));
+            if (p.world > 1) {           // into every rank's output buffer (peer memory over NVLink)
+                const size_t o = (size_t)m * p.n_total + p.col_offset + col_base + col;
+                for (int g = 0; g < p.world; ++g) p.peer_out[g][o] = h;
+            } else {
+                p.C[(size_t)m * p.N + col_base + col] = h;
+            }
         }
     }
     named_barrier(1, kMathThreads);
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* addr, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* addr) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
+
+// End of a CTA of a fused all-gather launch (thread 0).  Every CTA makes its
+// stores into peer memory visible system-wide; in a launch that ends a group
+// (barrier), the last CTA to finish publishes this rank's arrival -- the next
+// epoch -- in every rank's flags and waits (bounded) until every rank's
+// arrival for that epoch is in its own.  Earlier launches of the group ended
+// before this one passed griddepcontrol.wait, after their own fences, so one
+// epoch covers the whole group.  The stream's next kernel starts only after
+// this launch ends: it sees every rank's columns.
+__device__ __forceinline__ void gather_complete(const DecodeParams& p) {
+    __threadfence_system();
+    if (!p.barrier || atomicAdd(p.counter, 1u) != gridDim.x - 1) return;
+    atomicExch(p.counter, 0u);                       // no other CTA of this launch touches it again
+    const unsigned epoch = p.counter[1] + 1u;
+    p.counter[1] = epoch;
+    __threadfence_system();
+    for (int g = 0; g < p.world; ++g) st_release_sys(p.peer_flags[g] + p.rank, epoch);
+    const uint64_t t0 = global_timer_ns();
+    for (int q = 0; q < p.world; ++q) {
+        while ((int)(ld_acquire_sys(p.local_flags + q) - epoch) < 0) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(&g_decode_error, kErrTimeout);
+                return;
+            }
+        }
+    }
 }
 
 // MINB: CTAs per SM the register budget is sized for.  2 leaves room for the
@@ -689,6 +738,7 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
         for (int j = (issued > p.stages ? issued - p.stages : 0); j < issued; ++j)
             mbar_wait_bounded(&full[j % p.stages], (uint32_t)((j / p.stages) & 1), kWaitLimitNs / 4);
     }
+    if (p.world > 1 && tid == 0) gather_complete(p);
 }
 
 template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int MINB>
@@ -765,8 +815,8 @@ int decode_device_error(cudaStream_t stream, unsigned* out, bool clear) {
     return e == cudaSuccess ? T4B_OK : record_cuda_error(e);
 }
 
-int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
-                   int K, int group, cudaStream_t stream) {
+static int decode_impl(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M,
+                       int N, int K, int group, const T4BGather* gather, cudaStream_t stream) {
     const int KW = K / 8;
     const int gw = group / 8;
     if (M > 16 || (long long)M * K > 32768) return T4B_ERR_UNSUPPORTED;
@@ -808,6 +858,30 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
     p.sum_floats = (p.KWp / p.fb) * 8 * MT;
     p.red_floats = warps * 32 * M;
     p.kwdiv = make_fastdiv((uint32_t)p.KWp);
+    p.world = 1;
+    p.rank = 0;
+    p.n_total = N;
+    p.col_offset = 0;
+    p.barrier = 0;
+    p.local_flags = nullptr;
+    p.counter = nullptr;
+    for (int g = 0; g < 8; ++g) {
+        p.peer_out[g] = nullptr;
+        p.peer_flags[g] = nullptr;
+    }
+    if (gather) {
+        p.world = gather->world;
+        p.rank = gather->rank;
+        p.n_total = gather->n_total;
+        p.col_offset = gather->col_offset;
+        p.barrier = gather->barrier ? 1 : 0;
+        p.local_flags = gather->local_flags;
+        p.counter = gather->counter;
+        for (int g = 0; g < p.world; ++g) {
+            p.peer_out[g] = static_cast<uint16_t*>(gather->out[g]);
+            p.peer_flags[g] = gather->flags[g];
+        }
+    }
     const int weight_bytes = warps * 2048;
     p.slot_bytes = (weight_bytes + p.s_bytes * (Z ? 2 : 1) + 1023) / 1024 * 1024;
     const size_t fixed = 1024 + (size_t)p.act_bytes + 4 * (size_t)(p.sum_floats + p.red_floats) + kMaxStages * 16 + 8 + 16;
@@ -850,6 +924,21 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
         maps.z_split = maps.s_split;
     }
     return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, 2 * p.G <= sm_count(), maps, p, smem, stream);
+}
+
+int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
+                   int K, int group, cudaStream_t stream) {
+    return decode_impl(is_signed, A, W, S, Z, C, M, N, K, group, nullptr, stream);
+}
+
+int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const void* S, const void* Z, int M, int N,
+                          int K, int group, const T4BGather* g, cudaStream_t stream) {
+    if (!g || g->world < 2 || g->world > 8 || g->rank < 0 || g->rank >= g->world) return T4B_ERR_INVALID_VALUE;
+    if (g->col_offset < 0 || g->n_total < 1 || (long long)g->col_offset + N > g->n_total) return T4B_ERR_INVALID_VALUE;
+    if (!g->local_flags || !g->counter) return T4B_ERR_NULL_POINTER;
+    for (int r = 0; r < g->world; ++r)
+        if (!g->out[r] || !g->flags[r]) return T4B_ERR_NULL_POINTER;
+    return decode_impl(is_signed, A, W, S, Z, nullptr, M, N, K, group, g, stream);
 }
 
 }  // namespace t4b

@@ -4,19 +4,25 @@ The reference has no multi-GPU code; this is the one multi-GPU piece the
 library adds.  Rank r of a G-rank group holds columns [r*N/G, (r+1)*N/G) of
 every packed weight (word columns are sliced; the packed layout is unchanged)
 and the matching scale / zero-point columns.  A forward pass runs the
-single-GPU kernel on the local columns and gathers the G output slices with
-one ``all_gather_into_tensor`` over NCCL (NVLink / NVSwitch on a B200 node).
-Several projections that consume the same activation (q/k/v, gate/up) can
-share one gather (``ShardedGroup``), which matters at M = 1 where the gather's
-latency, not its bytes, dominates.
+single-GPU kernel on the local columns and gathers the G output slices:
+  * ``P2PGatherGroup``: the decode kernel stores its columns straight into
+    every rank's output buffer over NVLink and ends once every rank's columns
+    have arrived -- no collective call, so a whole step can be one CUDA graph;
+  * ``ShardedGroup``: one ``all_gather_into_tensor`` (NCCL on GPUs) after the
+    local kernels, for any shape and format.
+Several projections that consume the same activation (q/k/v, gate/up) share
+one gather, which matters at M = 1 where the gather's latency, not its bytes,
+dominates.
 
 Collectives are issued in the same order on every rank; no rank skips one.
 """
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 
 def shard_bounds(N, rank, world):
@@ -141,3 +147,126 @@ def unpack_gathered(gathered, widths):
         outs.append(part.permute(1, 0, 2).reshape(M, G * w))  # a copy only when M > 1 or several parts
         off += w
     return outs
+
+
+# ---------------------------------------------------------------- fused gather
+def column_offsets(widths, world):
+    """Start column of each projection in a group buffer: projection i holds
+    world * widths[i] columns, rank r's slice at offset + r * widths[i]."""
+    offs, off = [], 0
+    for w in widths:
+        offs.append(off)
+        off += world * w
+    return offs, off
+
+
+class _DeviceArray:
+    """Device memory exposed to torch without a copy (__cuda_array_interface__)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class P2PGatherGroup:
+    """Column-sharded projections that read the same activation, gathered by
+    the decode kernel itself instead of a collective: each rank's GEMV stores
+    its columns straight into every rank's output buffer (peer memory over
+    NVLink, mapped with CUDA IPC), and the group's last launch ends only when
+    every rank's columns have arrived (flags with bounded waits; see
+    t4b_fused_w4a16_gemv_allgather).  With no collective call in it, a step
+    made of these groups can be captured as one CUDA graph.
+
+    M is fixed (the buffers are allocated once).  The outputs are views of this
+    group's buffer and are overwritten by its next call.  Every rank must create
+    its groups in the same order and call them in the same order.  Raises
+    RuntimeError when the decode kernel does not take a shape (use
+    ShardedGroup, the NCCL path, then)."""
+
+    def __init__(self, linears, M, process_group=None):
+        self.linears = list(linears)
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        if not 2 <= self.world <= 8:
+            raise ValueError("the fused gather serves 2 to 8 ranks")
+        if any(lin.fmt not in ("s4", "u4") for lin in self.linears):
+            raise ValueError("the fused gather serves the W4A16 projections")
+        self.M = M
+        self.widths = [lin.n_local for lin in self.linears]
+        self.offsets, self.n_total = column_offsets(self.widths, self.world)
+        self.device = self.linears[0].W.device
+        lib = _lib.load()
+        self._lib = lib
+        self._own, self._opened = [], []
+        with torch.cuda.device(self.device):
+            out_ptr = self._alloc(M * self.n_total * 2)
+            flags_ptr = self._alloc(max(256, 4 * self.world))
+            counter_ptr = self._alloc(256)
+            handles = [self._handle(out_ptr), self._handle(flags_ptr)]
+            everyone = [None] * self.world
+            dist.all_gather_object(everyone, handles, group=process_group)
+            outs, flags = [], []
+            for g in range(self.world):
+                if g == self.rank:
+                    outs.append(out_ptr)
+                    flags.append(flags_ptr)
+                else:
+                    outs.append(self._open(everyone[g][0]))
+                    flags.append(self._open(everyone[g][1]))
+        self.out = torch.as_tensor(_DeviceArray(out_ptr, (M, self.n_total), "<f2"), device=self.device)
+        self._gathers = []
+        for i in range(len(self.linears)):
+            g = _lib.T4BGather()
+            for r in range(self.world):
+                g.out[r] = outs[r]
+                g.flags[r] = flags[r]
+            g.local_flags = flags_ptr
+            g.counter = counter_ptr
+            g.world, g.rank, g.n_total = self.world, self.rank, self.n_total
+            g.col_offset = self.offsets[i] + self.rank * self.widths[i]
+            g.barrier = 1 if i == len(self.linears) - 1 else 0
+            self._gathers.append(g)
+
+    def _alloc(self, nbytes):
+        p = ctypes.c_void_p()
+        _lib.check(self._lib.t4b_ipc_alloc(nbytes, ctypes.byref(p)), "t4b_ipc_alloc")
+        self._own.append(p.value)
+        return p.value
+
+    def _handle(self, ptr):
+        buf = ctypes.create_string_buffer(64)
+        _lib.check(self._lib.t4b_ipc_handle(ptr, buf), "t4b_ipc_handle")
+        return buf.raw
+
+    def _open(self, handle):
+        buf = ctypes.create_string_buffer(handle, 64)
+        p = ctypes.c_void_p()
+        _lib.check(self._lib.t4b_ipc_open(buf, ctypes.byref(p)), "t4b_ipc_open")
+        self._opened.append(p.value)
+        return p.value
+
+    def __call__(self, x):
+        if x.size(0) != self.M or x.dtype != torch.float16 or not x.is_contiguous():
+            raise RuntimeError(f"the fused gather group takes contiguous fp16 activations of {self.M} rows")
+        stream = torch._C._cuda_getCurrentRawStream(self.device.index)
+        fn = self._lib.t4b_fused_w4a16_gemv_allgather
+        for lin, g in zip(self.linears, self._gathers):
+            K = lin.W.size(0) * 8
+            S = lin.S if lin.S.dim() == 2 else lin.S.reshape(1, -1)
+            Z = lin.Z.data_ptr() if lin.Z is not None and lin.Z.numel() else None
+            st = fn(x.data_ptr(), lin.W.data_ptr(), S.data_ptr(), Z, self.M, lin.n_local, K, K // S.size(0),
+                    1 if lin.fmt == "s4" else 0, ctypes.byref(g), stream)
+            if st:
+                _lib.check(st, "t4b_fused_w4a16_gemv_allgather")
+        return [self.out[:, off:off + self.world * w] for off, w in zip(self.offsets, self.widths)]
+
+    def close(self):
+        """Release the peers' mappings and this rank's buffers.  Call on every
+        rank after a barrier, once no rank can still be writing."""
+        for p in self._opened:
+            self._lib.t4b_ipc_close(p)
+        for p in self._own:
+            self._lib.t4b_ipc_free(p)
+        self._opened, self._own = [], []
+        self.out = None

@@ -1,0 +1,77 @@
+"""Host side of the fused GEMV + all-gather (t4b_fused_w4a16_gemv_allgather,
+t4_cuda_b200.shard.P2PGatherGroup) without a GPU: the ctypes mirror of the
+T4BGather struct matches the C compiler's layout, the entry point rejects bad
+descriptors before touching the GPU, and the group's column layout."""
+
+import ctypes
+import os
+import shutil
+import subprocess
+
+import pytest
+
+from t4_cuda_b200 import _lib, shard
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _lib.load()
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_gather_struct_layout_matches_c(tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text(
+        "#include <stdio.h>\n#include <stddef.h>\n#include \"t4b200.h\"\n"
+        "int main(void) { printf(\"%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(T4BGather),"
+        " offsetof(T4BGather, out), offsetof(T4BGather, flags), offsetof(T4BGather, local_flags),"
+        " offsetof(T4BGather, counter), offsetof(T4BGather, world), offsetof(T4BGather, rank),"
+        " offsetof(T4BGather, n_total), offsetof(T4BGather, col_offset), offsetof(T4BGather, barrier));"
+        " return 0; }\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    c = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    G = _lib.T4BGather
+    py = [ctypes.sizeof(G)] + [getattr(G, f).offset for f in
+                               ("out", "flags", "local_flags", "counter", "world", "rank", "n_total",
+                                "col_offset", "barrier")]
+    assert py == c
+
+
+def _gather(world=2, rank=0, n_total=256, col_offset=0, fill=True):
+    g = _lib.T4BGather()
+    g.world, g.rank, g.n_total, g.col_offset, g.barrier = world, rank, n_total, col_offset, 1
+    if fill:
+        for r in range(min(world, 8)):
+            g.out[r] = 0x10000 * (r + 1)
+            g.flags[r] = 0x20000 * (r + 1)
+        g.local_flags = 0x80000
+        g.counter = 0x90000
+    return g
+
+
+def test_allgather_rejects_bad_descriptors(lib):
+    p = ctypes.c_void_p(0x100000)
+    call = lambda g, N=128: lib.t4b_fused_w4a16_gemv_allgather(p, p, p, None, 1, N, 4096, 128, 1,
+                                                               ctypes.byref(g) if g is not None else None, None)
+    assert call(None) == 2                                   # no descriptor
+    assert call(_gather(world=1)) == 1                       # a gather needs 2..8 ranks
+    assert call(_gather(world=9)) == 1
+    assert call(_gather(rank=2)) == 1                        # rank outside the group
+    assert call(_gather(col_offset=200)) == 1                # columns past the buffer's row
+    assert call(_gather(fill=False)) == 2                    # buffers / flags missing
+    assert lib.t4b_fused_w4a16_gemv_allgather(p, p, p, None, 1, 128, 100, 128, 1,
+                                              ctypes.byref(_gather()), None) == 1   # K not a multiple of 8
+
+
+def test_group_column_layout():
+    offs, total = shard.column_offsets([512, 128, 128], 8)
+    assert offs == [0, 4096, 5120] and total == 6144
+    # rank r's slice of projection i starts at offs[i] + r * width[i]
+    w, world = [512, 128, 128], 8
+    starts = sorted(o + r * wi for o, wi in zip(offs, w) for r in range(world))
+    ends = sorted(o + (r + 1) * wi for o, wi in zip(offs, w) for r in range(world))
+    assert starts[0] == 0 and ends[-1] == total
+    assert all(a == b for a, b in zip(ends[:-1], starts[1:]))     # slices tile the row exactly

@@ -423,6 +423,14 @@ def run_ours(args):
         e2e_ms = float(t.item())
     e2e_value = step_bytes * args.steps / (e2e_ms * 1e-3) / 1e9
 
+    # a bounded wait that ran out or a launch that aborted sets the library's
+    # device error word; the line reports it (max over ranks)
+    dev_err = int(ops.device_error(dev))
+    if dist is not None:
+        t = torch.tensor([dev_err], device=dev, dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_err = int(t.item())
+
     if use_graph:
         del graph
     torch.cuda.synchronize()
@@ -465,14 +473,18 @@ def run_ours(args):
                    "l2_policy": "weights rotate through a pool >= 4x L2 (inputs larger than L2)",
                    "parallelism": {"single GPU": "single GPU",
                                    "fused": f"column-shard x{world}, all-gather fused into the decode GEMV "
-                                            "(peer stores over NVLink, completion flags; whole step one CUDA graph)",
+                                            "(epoch-tagged column pairs stored into peer memory over NVLink; "
+                                            "whole step one CUDA graph)",
                                    "nccl": f"column-shard x{world} + NCCL all-gather (local projections of each "
                                            "gather group replayed as a CUDA graph, all-gathers from the host)"}[gather_mode],
                    "frac_of_8TBs": round(value / 8000.0, 4)},
         "gpu_launches": launches_per_step * args.steps,
+        "device_error": dev_err,
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
-                "api": "t4_kernels.fused_w4a16_gemm_s4 (eager, pinned host buffers)"},
+                "api": {"single GPU": "t4_kernels.fused_w4a16_gemm_s4",
+                        "fused": "t4_cuda_b200.shard.P2PGatherGroup (t4b_fused_w4a16_gemv_allgather)",
+                        "nccl": "t4_cuda_b200.shard.ShardedGroup"}[gather_mode] + " (eager, pinned host buffers)"},
         "per_shape": per_shape,
         "roofline": roof,
         "clocks": clk.summary(),

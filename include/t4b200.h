@@ -144,24 +144,26 @@ int t4b_fused_w4a16_gemv_noalloc(const void* A, const void* W_packed, const void
 /* ---- column-sharded decode GEMV with a fused all-gather over peer memory ---
  * No counterpart in the reference (it has no multi-GPU code).  Rank `rank` of
  * `world` GPUs (one process each) holds columns of a projection; instead of a
- * GEMV followed by an all-gather collective, the decode kernel stores each of
- * its output columns straight into every rank's output buffer (device pointers
- * of peer memory, opened with t4b_ipc_open), and the launch that ends a group
- * (barrier = 1) waits until every rank's columns have arrived: when it
- * completes, `out[rank]` holds the whole [M, n_total] output.
- *   out[g]        rank g's output buffer, row pitch n_total fp16 elements;
- *                 this rank writes columns col_offset .. col_offset + N - 1
- *   flags[g]      rank g's arrival flags (world uint32, zero at start)
- *   local_flags   this rank's flags (== flags[rank])
- *   counter       this rank's two uint32 (zero at start): CTAs done, epoch
- * Every rank must make the same sequence of calls on the same buffers.  Waits
- * are bounded (2 s); a rank that gives up sets the device error word.  Returns
+ * GEMV followed by an all-gather collective, the decode kernel stores each
+ * pair of its output columns, with the call's epoch, as one 64-bit word into
+ * every rank's receive buffer (device pointers of peer memory, opened with
+ * t4b_ipc_open).  The words validate themselves, so no fence or flag is
+ * needed.  Several calls (projections that share an activation) form a group;
+ * its last call (barrier = 1) ends only when the whole group has arrived in
+ * this rank's receive buffer, and then `out` holds the [M, n_total] output.
+ *   recv[g]      rank g's receive buffer: 2 halves (epoch parity) of
+ *                M x n_total/2 64-bit words, zero at start
+ *   out          this rank's gathered output, [M, n_total] fp16 (local)
+ *   counter      this rank's two uint32 (zero at start): CTAs done, epoch
+ *   col_offset   first column this rank writes (even); n_total even
+ * Every rank makes the same sequence of calls on the same buffers; a call's
+ * epoch is the group's count of completed groups + 1.  Waits are bounded
+ * (2 s); a rank that gives up sets the device error word.  Returns
  * T4B_ERR_UNSUPPORTED (nothing launched) for shapes the decode kernel does not
  * take; the caller then falls back to its collective. */
 typedef struct {
-    void* out[8];
-    unsigned* flags[8];
-    unsigned* local_flags;
+    void* recv[8];
+    void* out;
     unsigned* counter;
     int world, rank, n_total, col_offset, barrier;
 } T4BGather;

@@ -34,11 +34,10 @@ SIGNATURES = {
 
 
 class T4BGather(ctypes.Structure):
-    """include/t4b200.h T4BGather: peer output buffers and flags of a fused all-gather."""
+    """include/t4b200.h T4BGather: receive buffers, output and counter of a fused all-gather."""
     _fields_ = [
-        ("out", _vp * 8),
-        ("flags", _vp * 8),
-        ("local_flags", _vp),
+        ("recv", _vp * 8),
+        ("out", _vp),
         ("counter", _vp),
         ("world", ctypes.c_int),
         ("rank", ctypes.c_int),

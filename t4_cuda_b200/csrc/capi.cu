@@ -221,6 +221,7 @@ int t4b_ipc_alloc(size_t bytes, void** ptr) {
     *ptr = nullptr;
     cudaError_t e = cudaMalloc(ptr, bytes);
     if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();   // zeroed before any peer can map it
     return e == cudaSuccess ? T4B_OK : t4b::record_cuda_error(e);
 }
 

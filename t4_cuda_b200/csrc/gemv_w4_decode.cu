@@ -96,11 +96,11 @@ struct DecodeParams {
     int sum_floats;     // flush-block activation sums
     int red_floats;     // cross-warp reduction buffer
     FastDiv kwdiv;      // division by KWp
-    // fused all-gather (world > 1): each output column goes to every rank's buffer
-    uint16_t* peer_out[8];
-    unsigned* peer_flags[8];
-    unsigned* local_flags;
-    unsigned* counter;
+    // fused all-gather (world > 1): each pair of output columns goes, with the
+    // call's epoch, as one 64-bit word to every rank's receive buffer
+    unsigned long long* recv[8];
+    uint32_t* gout;         // this rank's gathered output (column pairs)
+    unsigned* counter;      // [0] CTAs of a group's last launch done, [1] groups done
     int world, rank, n_total, col_offset, barrier;
 };
 
@@ -338,6 +338,16 @@ __device__ __forceinline__ void arrive_a(uint32_t bar) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
 }
 
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* addr, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* addr) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+    return v;
+}
+
 // State the math warps carry from one tile group to the next.
 struct MathCtx {
     uint32_t ring_a, act_a, sums_a, pitch16;
@@ -347,6 +357,7 @@ struct MathCtx {
     int warp, lane, r, c, bb, L;
     int slot;
     uint32_t phase;
+    uint32_t epoch;         // fused all-gather: this call's epoch (0 on one GPU)
     bool aborted;
 };
 
@@ -512,56 +523,79 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
     for (int pair = x.warp; pair < nwc * M; pair += kWarps) {
         const int w = pair / M, m = pair - w * M;
         const int col = 32 * w + x.lane;
+        uint32_t hv = 0;
         if (col < ncols) {
             float v = 0.f;
             for (int k = 0; k < rbs; ++k) v += red[((w * rbs + k) * 32 + x.lane) * M + m];
             if (kSplitGroup)     // the second row half sits in columns 16..31 of each row block
                 for (int k = 0; k < rbs; ++k) v += red[(k * 32 + x.lane + kBoxCols) * M + m];
             const uint16_t h = __half_as_ushort(__float2half_rn(v));
-            if (p.world > 1) {           // into every rank's output buffer (peer memory over NVLink)
-                const size_t o = (size_t)m * p.n_total + p.col_offset + col_base + col;
-                for (int g = 0; g < p.world; ++g) p.peer_out[g][o] = h;
-            } else {
-                p.C[(size_t)m * p.N + col_base + col] = h;
+            if (p.world == 1) p.C[(size_t)m * p.N + col_base + col] = h;
+            hv = h;
+        }
+        if (p.world > 1) {
+            // Even lanes pair their column with the next one (ncols is even,
+            // and every lane of the warp runs this iteration) and store
+            // {col, col+1, epoch} as one word into every rank's receive buffer
+            // (peer memory over NVLink): a reader that sees the epoch sees
+            // the data, so no fence or flag is needed.
+            const uint32_t hi = __shfl_down_sync(0xffffffffu, hv, 1);
+            if (col < ncols && (x.lane & 1) == 0) {
+                const unsigned long long word = ((unsigned long long)x.epoch << 32) | (hv | (hi << 16));
+                const size_t o = ((size_t)(x.epoch & 1u) * M + m) * (size_t)(p.n_total >> 1) +
+                                 (size_t)((p.col_offset + col_base + col) >> 1);
+                for (int g = 0; g < p.world; ++g) st_relaxed_sys_u64(p.recv[g] + o, word);
             }
         }
     }
     named_barrier(1, kMathThreads);
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* addr, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* addr) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-    return v;
-}
-
-// End of a CTA of a fused all-gather launch (thread 0).  Every CTA makes its
-// stores into peer memory visible system-wide; in a launch that ends a group
-// (barrier), the last CTA to finish publishes this rank's arrival -- the next
-// epoch -- in every rank's flags and waits (bounded) until every rank's
-// arrival for that epoch is in its own.  Earlier launches of the group ended
-// before this one passed griddepcontrol.wait, after their own fences, so one
-// epoch covers the whole group.  The stream's next kernel starts only after
-// this launch ends: it sees every rank's columns.
+// End of a CTA of the launch that closes a fused all-gather group (every
+// thread).  The CTA's slice of the group's words in this rank's receive
+// buffer is polled until each carries this call's epoch (bounded), and the
+// column pairs go to the local output.  Every CTA of the launch is resident
+// at once (the grid is at most one CTA per SM), so a CTA waiting here never
+// keeps the CTAs that produce its words from running.  The last CTA to finish
+// advances the epoch: every CTA of the launch read it before arriving, and
+// the next call reads it only after this launch has ended.
 __device__ __forceinline__ void gather_complete(const DecodeParams& p) {
-    __threadfence_system();
-    if (!p.barrier || atomicAdd(p.counter, 1u) != gridDim.x - 1) return;
-    atomicExch(p.counter, 0u);                       // no other CTA of this launch touches it again
-    const unsigned epoch = p.counter[1] + 1u;
-    p.counter[1] = epoch;
-    __threadfence_system();
-    for (int g = 0; g < p.world; ++g) st_release_sys(p.peer_flags[g] + p.rank, epoch);
+    const uint32_t epoch = *reinterpret_cast<volatile const unsigned*>(p.counter + 1) + 1u;
+    const int words = p.M * (p.n_total >> 1);
+    const int per = (words + gridDim.x - 1) / gridDim.x;
+    const int lo = blockIdx.x * per;
+    const int hi = lo + per < words ? lo + per : words;
+    const unsigned long long* src = p.recv[p.rank] + (size_t)(epoch & 1u) * words;
+    constexpr int kBatch = 4;
     const uint64_t t0 = global_timer_ns();
-    for (int q = 0; q < p.world; ++q) {
-        while ((int)(ld_acquire_sys(p.local_flags + q) - epoch) < 0) {
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
-                atomicOr(&g_decode_error, kErrTimeout);
-                return;
+    bool ok = true;
+    for (int base = lo + (int)threadIdx.x; ok && base < hi; base += kBatch * blockDim.x) {
+        unsigned long long v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * (int)blockDim.x;
+            v[u] = i < hi ? ld_relaxed_sys_u64(src + i) : ((unsigned long long)epoch << 32);
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * (int)blockDim.x;
+            while (ok && (uint32_t)(v[u] >> 32) != epoch) {
+                if (global_timer_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(&g_decode_error, kErrTimeout);
+                    ok = false;
+                } else {
+                    v[u] = ld_relaxed_sys_u64(src + i);
+                }
             }
+            if (ok && i < hi) p.gout[i] = (uint32_t)v[u];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();     // this CTA's read of the epoch is done before it arrives
+        if (atomicAdd(p.counter, 1u) == gridDim.x - 1) {
+            p.counter[0] = 0u;
+            p.counter[1] = epoch;
         }
     }
 }
@@ -661,11 +695,13 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     x.sflag = sflag;
     x.slot = 0;
     x.phase = 0;
+    x.epoch = 0;
     x.aborted = false;
     GroupInfo gi = group_info(p, q, 0);
     LaneOffsets<MT> lo = setup_any<MT>(gi.kind, p, x);
 
     pdl_wait_prior_grid();     // A and C may belong to the previous kernel
+    if (p.world > 1) x.epoch = *reinterpret_cast<volatile const unsigned*>(p.counter + 1) + 1u;
 
     // ---- resident activations: permuted records + flush-block sums.  Every
     // thread issues kPrep independent loads before using any, so the prologue
@@ -738,7 +774,7 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
         for (int j = (issued > p.stages ? issued - p.stages : 0); j < issued; ++j)
             mbar_wait_bounded(&full[j % p.stages], (uint32_t)((j / p.stages) & 1), kWaitLimitNs / 4);
     }
-    if (p.world > 1 && tid == 0) gather_complete(p);
+    if (p.world > 1 && p.barrier) gather_complete(p);
 }
 
 template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int MINB>
@@ -863,24 +899,18 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
     p.n_total = N;
     p.col_offset = 0;
     p.barrier = 0;
-    p.local_flags = nullptr;
+    p.gout = nullptr;
     p.counter = nullptr;
-    for (int g = 0; g < 8; ++g) {
-        p.peer_out[g] = nullptr;
-        p.peer_flags[g] = nullptr;
-    }
+    for (int g = 0; g < 8; ++g) p.recv[g] = nullptr;
     if (gather) {
         p.world = gather->world;
         p.rank = gather->rank;
         p.n_total = gather->n_total;
         p.col_offset = gather->col_offset;
         p.barrier = gather->barrier ? 1 : 0;
-        p.local_flags = gather->local_flags;
+        p.gout = static_cast<uint32_t*>(gather->out);
         p.counter = gather->counter;
-        for (int g = 0; g < p.world; ++g) {
-            p.peer_out[g] = static_cast<uint16_t*>(gather->out[g]);
-            p.peer_flags[g] = gather->flags[g];
-        }
+        for (int g = 0; g < p.world; ++g) p.recv[g] = static_cast<unsigned long long*>(gather->recv[g]);
     }
     const int weight_bytes = warps * 2048;
     p.slot_bytes = (weight_bytes + p.s_bytes * (Z ? 2 : 1) + 1023) / 1024 * 1024;
@@ -934,10 +964,15 @@ int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, 
 int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const void* S, const void* Z, int M, int N,
                           int K, int group, const T4BGather* g, cudaStream_t stream) {
     if (!g || g->world < 2 || g->world > 8 || g->rank < 0 || g->rank >= g->world) return T4B_ERR_INVALID_VALUE;
-    if (g->col_offset < 0 || g->n_total < 1 || (long long)g->col_offset + N > g->n_total) return T4B_ERR_INVALID_VALUE;
-    if (!g->local_flags || !g->counter) return T4B_ERR_NULL_POINTER;
-    for (int r = 0; r < g->world; ++r)
-        if (!g->out[r] || !g->flags[r]) return T4B_ERR_NULL_POINTER;
+    if (g->col_offset < 0 || g->n_total < 2 || (long long)g->col_offset + N > g->n_total) return T4B_ERR_INVALID_VALUE;
+    if ((g->col_offset | g->n_total | N) & 1) return T4B_ERR_INVALID_VALUE;     // whole column pairs
+    if ((long long)M * g->n_total >= (1ll << 31)) return T4B_ERR_INVALID_VALUE;
+    if (!g->out || !g->counter) return T4B_ERR_NULL_POINTER;
+    if (reinterpret_cast<uintptr_t>(g->out) & 3) return T4B_ERR_MISALIGNED;
+    for (int r = 0; r < g->world; ++r) {
+        if (!g->recv[r]) return T4B_ERR_NULL_POINTER;
+        if (reinterpret_cast<uintptr_t>(g->recv[r]) & 7) return T4B_ERR_MISALIGNED;
+    }
     return decode_impl(is_signed, A, W, S, Z, nullptr, M, N, K, group, g, stream);
 }
 

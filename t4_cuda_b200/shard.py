@@ -6,8 +6,9 @@ every packed weight (word columns are sliced; the packed layout is unchanged)
 and the matching scale / zero-point columns.  A forward pass runs the
 single-GPU kernel on the local columns and gathers the G output slices:
   * ``P2PGatherGroup``: the decode kernel stores its columns straight into
-    every rank's output buffer over NVLink and ends once every rank's columns
-    have arrived -- no collective call, so a whole step can be one CUDA graph;
+    every rank's receive buffer over NVLink, and a group's last launch ends
+    once every rank's columns have arrived -- no collective call, so a whole
+    step can be one CUDA graph;
   * ``ShardedGroup``: one ``all_gather_into_tensor`` (NCCL on GPUs) after the
     local kernels, for any shape and format.
 Several projections that consume the same activation (q/k/v, gate/up) share
@@ -160,28 +161,22 @@ def column_offsets(widths, world):
     return offs, off
 
 
-class _DeviceArray:
-    """Device memory exposed to torch without a copy (__cuda_array_interface__)."""
-
-    def __init__(self, ptr, shape, typestr):
-        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
-                                         "version": 3, "strides": None}
-
-
 class P2PGatherGroup:
     """Column-sharded projections that read the same activation, gathered by
     the decode kernel itself instead of a collective: each rank's GEMV stores
-    its columns straight into every rank's output buffer (peer memory over
-    NVLink, mapped with CUDA IPC), and the group's last launch ends only when
-    every rank's columns have arrived (flags with bounded waits; see
+    its column pairs, tagged with the call's epoch, straight into every rank's
+    receive buffer (peer memory over NVLink, mapped with CUDA IPC); the
+    group's last launch polls this rank's receive buffer until the whole group
+    has arrived and writes the local output (bounded waits; see
     t4b_fused_w4a16_gemv_allgather).  With no collective call in it, a step
     made of these groups can be captured as one CUDA graph.
 
     M is fixed (the buffers are allocated once).  The outputs are views of this
-    group's buffer and are overwritten by its next call.  Every rank must create
-    its groups in the same order and call them in the same order.  Raises
-    RuntimeError when the decode kernel does not take a shape (use
-    ShardedGroup, the NCCL path, then)."""
+    rank's output buffer, written only by this rank's own calls, and are
+    overwritten by the group's next call.  Every rank must create its groups
+    in the same order and call them in the same order.  Raises RuntimeError
+    when the decode kernel does not take a shape (use ShardedGroup, the NCCL
+    path, then)."""
 
     def __init__(self, linears, M, process_group=None):
         self.linears = list(linears)
@@ -194,35 +189,28 @@ class P2PGatherGroup:
             raise ValueError("the fused gather serves the W4A16 projections")
         self.M = M
         self.widths = [lin.n_local for lin in self.linears]
+        if any(w % 2 for w in self.widths):
+            raise ValueError("the fused gather moves column pairs: every shard width must be even")
         self.offsets, self.n_total = column_offsets(self.widths, self.world)
         self.device = self.linears[0].W.device
         lib = _lib.load()
         self._lib = lib
         self._own, self._opened = [], []
+        self.out = torch.empty((M, self.n_total), dtype=torch.float16, device=self.device)
+        self.counter = torch.zeros(2, dtype=torch.int32, device=self.device)
         with torch.cuda.device(self.device):
-            out_ptr = self._alloc(M * self.n_total * 2)
-            flags_ptr = self._alloc(max(256, 4 * self.world))
-            counter_ptr = self._alloc(256)
-            handles = [self._handle(out_ptr), self._handle(flags_ptr)]
+            # receive buffer: two halves (epoch parity) of M x n_total/2 64-bit words
+            recv_ptr = self._alloc(M * self.n_total * 8)
             everyone = [None] * self.world
-            dist.all_gather_object(everyone, handles, group=process_group)
-            outs, flags = [], []
-            for g in range(self.world):
-                if g == self.rank:
-                    outs.append(out_ptr)
-                    flags.append(flags_ptr)
-                else:
-                    outs.append(self._open(everyone[g][0]))
-                    flags.append(self._open(everyone[g][1]))
-        self.out = torch.as_tensor(_DeviceArray(out_ptr, (M, self.n_total), "<f2"), device=self.device)
+            dist.all_gather_object(everyone, self._handle(recv_ptr), group=process_group)
+            recv = [recv_ptr if g == self.rank else self._open(everyone[g]) for g in range(self.world)]
         self._gathers = []
         for i in range(len(self.linears)):
             g = _lib.T4BGather()
             for r in range(self.world):
-                g.out[r] = outs[r]
-                g.flags[r] = flags[r]
-            g.local_flags = flags_ptr
-            g.counter = counter_ptr
+                g.recv[r] = recv[r]
+            g.out = self.out.data_ptr()
+            g.counter = self.counter.data_ptr()
             g.world, g.rank, g.n_total = self.world, self.rank, self.n_total
             g.col_offset = self.offsets[i] + self.rank * self.widths[i]
             g.barrier = 1 if i == len(self.linears) - 1 else 0
@@ -269,4 +257,3 @@ class P2PGatherGroup:
         for p in self._own:
             self._lib.t4b_ipc_free(p)
         self._opened, self._own = [], []
-        self.out = None

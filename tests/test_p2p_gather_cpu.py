@@ -25,8 +25,8 @@ def test_gather_struct_layout_matches_c(tmp_path):
     src = tmp_path / "layout.c"
     src.write_text(
         "#include <stdio.h>\n#include <stddef.h>\n#include \"t4b200.h\"\n"
-        "int main(void) { printf(\"%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(T4BGather),"
-        " offsetof(T4BGather, out), offsetof(T4BGather, flags), offsetof(T4BGather, local_flags),"
+        "int main(void) { printf(\"%zu %zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(T4BGather),"
+        " offsetof(T4BGather, recv), offsetof(T4BGather, out),"
         " offsetof(T4BGather, counter), offsetof(T4BGather, world), offsetof(T4BGather, rank),"
         " offsetof(T4BGather, n_total), offsetof(T4BGather, col_offset), offsetof(T4BGather, barrier));"
         " return 0; }\n")
@@ -35,7 +35,7 @@ def test_gather_struct_layout_matches_c(tmp_path):
     c = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     G = _lib.T4BGather
     py = [ctypes.sizeof(G)] + [getattr(G, f).offset for f in
-                               ("out", "flags", "local_flags", "counter", "world", "rank", "n_total",
+                               ("recv", "out", "counter", "world", "rank", "n_total",
                                 "col_offset", "barrier")]
     assert py == c
 
@@ -45,9 +45,8 @@ def _gather(world=2, rank=0, n_total=256, col_offset=0, fill=True):
     g.world, g.rank, g.n_total, g.col_offset, g.barrier = world, rank, n_total, col_offset, 1
     if fill:
         for r in range(min(world, 8)):
-            g.out[r] = 0x10000 * (r + 1)
-            g.flags[r] = 0x20000 * (r + 1)
-        g.local_flags = 0x80000
+            g.recv[r] = 0x10000 * (r + 1)
+        g.out = 0x80000
         g.counter = 0x90000
     return g
 
@@ -61,7 +60,9 @@ def test_allgather_rejects_bad_descriptors(lib):
     assert call(_gather(world=9)) == 1
     assert call(_gather(rank=2)) == 1                        # rank outside the group
     assert call(_gather(col_offset=200)) == 1                # columns past the buffer's row
-    assert call(_gather(fill=False)) == 2                    # buffers / flags missing
+    assert call(_gather(col_offset=1)) == 1                  # column pairs: offsets even
+    assert call(_gather(n_total=255)) == 1
+    assert call(_gather(fill=False)) == 2                    # buffers missing
     assert lib.t4b_fused_w4a16_gemv_allgather(p, p, p, None, 1, 128, 100, 128, 1,
                                               ctypes.byref(_gather()), None) == 1   # K not a multiple of 8
 

@@ -17,6 +17,10 @@ column-sharded N ways and the outputs are gathered by the decode kernel itself
 (peer stores over NVLink, t4_cuda_b200.shard.P2PGatherGroup; --nccl-gather
 uses NCCL all-gather instead): the same token, so "scaling" is "strong".
 
+The line also carries "sharded_70b": Llama-3-70B layer projections
+column-sharded over the same N GPUs at M in {1, 16, 256, 4096} (see
+sharded_70b).
+
 --impl reference times the reference's CPU dequant + matmul path
 (tests/test_fused_gemm_correctness.py:22-36, restated in oracle/cpu_path.py)
 on the host cores, one projection per step.
@@ -43,6 +47,11 @@ PROJ = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 409
 # projections that read the same activation share one all-gather
 GATHERS = [("x", ["q", "k", "v"]), ("attn", ["o"]), ("x", ["gate", "up"]), ("h", ["down"])]
 ACT_K = {"x": 4096, "attn": 4096, "h": 14336}
+# Llama-3-70B layer: hidden 8192, intermediate 28672, 64 query / 8 KV heads of 128
+PROJ_70B = [("q", 8192, 8192), ("k", 8192, 1024), ("v", 8192, 1024), ("o", 8192, 8192),
+            ("gate", 8192, 28672), ("up", 8192, 28672), ("down", 28672, 8192)]
+ACT_K_70B = {"x": 8192, "attn": 8192, "h": 28672}
+M_70B = (1, 16, 256, 4096)
 
 
 def alg_bytes(M, K, N, group=GROUP):
@@ -257,6 +266,131 @@ def int3_and_dequant(dev):
     return out
 
 
+def _max_over_ranks(dist, dev, ms):
+    if dist is None:
+        return ms
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sharded_70b(dev, world, rank, dist, l2, nccl_gather=False, steps=10, warmup=3):
+    """Llama-3-70B layer projections column-sharded over the ranks at
+    M in {1, 16, 256, 4096}; one step = the seven projections of a layer with
+    every output gathered to every rank (max over ranks, CUDA events).
+    M <= 16 rotates the layers' weights through a pool >= 4x L2 and reports
+    HBM GB/s (algorithmic bytes of the full, unsharded layer); M >= 256 runs
+    one layer and reports TFLOP/s (2 M K N).  Gathers: the decode kernel's own
+    (P2PGatherGroup; the whole step one CUDA graph) where it takes the shape,
+    else one NCCL all-gather per group from the host (ShardedGroup; the local
+    projections of a group as one CUDA graph at M <= 16)."""
+    from t4_cuda_b200 import ops
+    from t4_cuda_b200.shard import P2PGatherGroup, ShardedGroup, ShardedLinear
+
+    gen = torch.Generator(device=dev).manual_seed(4 + 1000 * rank)
+
+    def make():
+        L = {}
+        for name, K, N in PROJ_70B:
+            n = N // world
+            W = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, n), dtype=torch.int32, device=dev, generator=gen)
+            S = (torch.randn((K // GROUP, n), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+            L[name] = ShardedLinear(W, S, None, "s4")
+        return L
+
+    layer_bytes_local = sum(K * (N // world) // 2 + (K // GROUP) * (N // world) * 2 for _, K, N in PROJ_70B)
+    pool = min(16, max(2, math.ceil(4 * l2 / layer_bytes_local)))
+    layers = [make() for _ in range(pool)]
+
+    def time_steps(run, reps):
+        for _ in range(warmup):
+            run()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        e1.synchronize()
+        return _max_over_ranks(dist, dev, e0.elapsed_time(e1) / reps)
+
+    cases = {}
+    for M in M_70B:
+        acts = {a: torch.randn((M, k), device=dev, generator=gen).half() for a, k in ACT_K_70B.items()}
+        decode = M <= 16
+        use = layers if decode else layers[:1]
+        mode, groups, graph = "single GPU", None, None
+        if world > 1 and decode and not nccl_gather:
+            built = []
+            try:
+                for L in use:
+                    built.append([])
+                    for _, names in GATHERS:
+                        built[-1].append(P2PGatherGroup([L[n] for n in names], M))
+                groups, mode = built, "fused"
+            except RuntimeError:     # the same shapes on every rank: every rank falls back together
+                for row in built:    # nothing was launched on these buffers
+                    for grp in row:
+                        grp.close()
+        if world > 1 and groups is None:
+            groups = [[ShardedGroup([L[n] for n in names]) for _, names in GATHERS] for L in use]
+            mode = "nccl"
+            if decode:
+                for row in groups:
+                    for g, (a, _) in enumerate(GATHERS):
+                        row[g].capture_local(acts[a])
+
+        def step():
+            for li, L in enumerate(use):
+                for g, (a, names) in enumerate(GATHERS):
+                    if groups is None:
+                        for n in names:
+                            ops.fused_w4a16_gemm_s4(acts[a], L[n].W, L[n].S, None)
+                    else:
+                        groups[li][g](acts[a])
+
+        run = step
+        if decode and mode != "nccl":
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                step()
+                step()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            run = graph.replay
+        ms = time_steps(run, steps if decode else 3)
+        per_layer = ms / len(use)
+        case = {"gather": mode, "ms_per_layer": round(per_layer, 4), "layers_per_step": len(use)}
+        if decode:
+            byts = sum(alg_bytes(M, K, N) for _, K, N in PROJ_70B)
+            case["GB/s"] = round(byts / (per_layer * 1e-3) / 1e9, 1)
+        else:
+            flops = sum(2.0 * M * K * N for _, K, N in PROJ_70B)
+            case["TFLOP/s"] = round(flops / (per_layer * 1e-3) / 1e12, 1)
+        cases[f"M={M}"] = case
+        del graph
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()       # no rank still writes into another's gather buffers
+        if groups is not None:
+            for row in groups:
+                for grp in row:
+                    if isinstance(grp, P2PGatherGroup):
+                        grp.close()
+                    else:
+                        grp.release_graph()
+        torch.cuda.synchronize()
+    return {"workload": "Llama-3-70B layer projections (q 8192x8192, k/v 8192x1024, o 8192x8192, "
+                        "gate/up 8192x28672, down 28672x8192), s4 g128, column-sharded", "n_gpus": world,
+            "distinct_weight_layers": pool, "weight_pool_bytes_per_gpu": pool * layer_bytes_local,
+            "scaling": "strong", "cases": cases}
+
+
 def run_ours(args):
     from t4_cuda_b200 import ops
     from t4_cuda_b200.shard import P2PGatherGroup, ShardedGroup, ShardedLinear
@@ -431,6 +565,10 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_err = int(t.item())
 
+    sh70 = None
+    if not args.no_70b:
+        sh70 = sharded_70b(dev, world, rank, dist, l2, nccl_gather=args.nccl_gather)
+
     if use_graph:
         del graph
     torch.cuda.synchronize()
@@ -498,6 +636,8 @@ def run_ours(args):
         line["gemm"] = gemm
     if others is not None:
         line["other_kernels"] = others
+    if sh70 is not None:
+        line["sharded_70b"] = sh70
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
     print(json.dumps(line), flush=True)
@@ -612,6 +752,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nccl-gather", action="store_true", help="N > 1: NCCL all-gather instead of the fused one")
+    ap.add_argument("--no-70b", action="store_true", help="skip the column-sharded Llama-3-70B layer section")
     ap.add_argument("--case", help="profiling driver: decode:K:N:M or gemm:M:K:N (a few launches, no JSON)")
     ap.add_argument("--launches", type=int, default=6, help="launches for --case")
     args = ap.parse_args()

@@ -168,6 +168,11 @@ typedef struct {
     int world, rank, n_total, col_offset, barrier;
 } T4BGather;
 
+/* T4B_OK when t4b_fused_w4a16_gemv_allgather takes a shape (this rank's N
+ * columns), T4B_ERR_UNSUPPORTED when it does not; launches nothing, but reads
+ * the current device's SM count. */
+int t4b_fused_w4a16_gemv_allgather_supported(int M, int N, int K, int group_size, int has_zero_points);
+
 int t4b_fused_w4a16_gemv_allgather(const void* A, const void* W_packed, const void* scales,
                                    const void* zero_points, int M, int N, int K, int group_size,
                                    int is_signed, const T4BGather* gather, void* stream);

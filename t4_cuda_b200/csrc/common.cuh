@@ -34,9 +34,11 @@ int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, 
 // T4B_ERR_UNSUPPORTED (without launching) for shapes it does not take.
 int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
                    int K, int group, cudaStream_t stream);
-// Same kernel with the fused all-gather of T4BGather (outputs into every
-// rank's buffer, completion flags); T4B_ERR_UNSUPPORTED where the decode
-// kernel does not apply.
+// T4B_OK when the decode kernel takes the shape (nothing is launched).
+int gemv_w4_decode_supported(int M, int N, int K, int group, bool has_zero_points);
+// Same kernel with the fused all-gather of T4BGather (epoch-tagged column
+// pairs into every rank's receive buffer); T4B_ERR_UNSUPPORTED where the
+// decode kernel does not apply.
 int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const void* S, const void* Z, int M, int N,
                           int K, int group, const T4BGather* g, cudaStream_t stream);
 

@@ -343,6 +343,13 @@ int t4b_fused_w4a16_gemm_s4(const void* A, const void* W_packed, const void* sca
     return t4b::fused_gemm<true>(A, W_packed, scales, zero_points, C, M, N, K, group_size, stream);
 }
 
+int t4b_fused_w4a16_gemv_allgather_supported(int M, int N, int K, int group_size, int has_zero_points) {
+    if (M < 1 || N < 1 || K < 8 || (K % 8) != 0) return T4B_ERR_INVALID_VALUE;
+    if (group_size < 8 || (group_size % 8) != 0 || (K % group_size) != 0) return T4B_ERR_INVALID_VALUE;
+    if (N & 1) return T4B_ERR_UNSUPPORTED;       // whole column pairs
+    return t4b::gemv_w4_decode_supported(M, N, K, group_size, has_zero_points != 0);
+}
+
 int t4b_fused_w4a16_gemv_allgather(const void* A, const void* W_packed, const void* scales, const void* zero_points,
                                    int M, int N, int K, int group_size, int is_signed, const T4BGather* gather,
                                    void* stream) {

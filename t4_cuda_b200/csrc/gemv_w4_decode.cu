@@ -851,8 +851,11 @@ int decode_device_error(cudaStream_t stream, unsigned* out, bool clear) {
     return e == cudaSuccess ? T4B_OK : record_cuda_error(e);
 }
 
+// plan_only: run every check and the shared-memory plan, launch nothing (the
+// pointers are not read; Z only says whether there are zero points).
 static int decode_impl(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M,
-                       int N, int K, int group, const T4BGather* gather, cudaStream_t stream) {
+                       int N, int K, int group, const T4BGather* gather, cudaStream_t stream,
+                       bool plan_only = false) {
     const int KW = K / 8;
     const int gw = group / 8;
     if (M > 16 || (long long)M * K > 32768) return T4B_ERR_UNSUPPORTED;
@@ -926,6 +929,7 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
         if (stages > kMaxStages) stages = kMaxStages;
     }
     if (stages < 2) return T4B_ERR_UNSUPPORTED;
+    if (plan_only) return T4B_OK;
     p.stages = stages;
     // A CTA whose weights fit in the ring fetches all of them before the
     // previous kernel ends.  One that must stream more than a ring's worth
@@ -959,6 +963,12 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
 int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
                    int K, int group, cudaStream_t stream) {
     return decode_impl(is_signed, A, W, S, Z, C, M, N, K, group, nullptr, stream);
+}
+
+int gemv_w4_decode_supported(int M, int N, int K, int group, bool has_zero_points) {
+    // a stand-in zero-point pointer: only its presence matters to the plan
+    const void* z = has_zero_points ? reinterpret_cast<const void*>(uintptr_t{256}) : nullptr;
+    return decode_impl(true, nullptr, nullptr, nullptr, z, nullptr, M, N, K, group, nullptr, nullptr, true);
 }
 
 int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const void* S, const void* Z, int M, int N,

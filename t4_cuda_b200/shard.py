@@ -195,6 +195,15 @@ class P2PGatherGroup:
         self.device = self.linears[0].W.device
         lib = _lib.load()
         self._lib = lib
+        with torch.cuda.device(self.device):
+            for lin in self.linears:
+                K = lin.W.size(0) * 8
+                groups = lin.S.size(0) if lin.S.dim() == 2 else 1
+                st = lib.t4b_fused_w4a16_gemv_allgather_supported(
+                    M, lin.n_local, K, K // groups, int(lin.Z is not None and lin.Z.numel() > 0))
+                if st:
+                    raise RuntimeError(f"the fused gather does not take M={M}, K={K}, N={lin.n_local} "
+                                       f"({lib.t4b_status_string(st).decode()}); use ShardedGroup")
         self._own, self._opened = [], []
         self.out = torch.empty((M, self.n_total), dtype=torch.float16, device=self.device)
         self.counter = torch.zeros(2, dtype=torch.int32, device=self.device)

@@ -76,3 +76,12 @@ def test_group_column_layout():
     ends = sorted(o + (r + 1) * wi for o, wi in zip(offs, w) for r in range(world))
     assert starts[0] == 0 and ends[-1] == total
     assert all(a == b for a, b in zip(ends[:-1], starts[1:]))     # slices tile the row exactly
+
+
+def test_support_query_rejects_bad_shapes(lib):
+    q = lib.t4b_fused_w4a16_gemv_allgather_supported
+    assert q(0, 256, 4096, 128, 0) == 1          # M < 1
+    assert q(1, 256, 4100, 128, 0) == 1          # K not a multiple of the group
+    assert q(1, 256, 4096, 12, 0) == 1           # group not a multiple of 8
+    assert q(1, 255, 4096, 128, 0) == 4          # odd width: no whole column pairs
+    assert q(17, 256, 4096, 128, 0) == 4         # M > 16: not a decode shape

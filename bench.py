@@ -17,7 +17,8 @@ column-sharded N ways and the outputs are gathered by the decode kernel itself
 (peer stores over NVLink, t4_cuda_b200.shard.P2PGatherGroup; --nccl-gather
 uses NCCL all-gather instead): the same token, so "scaling" is "strong".
 
-The line also carries "sharded_70b": Llama-3-70B layer projections
+The line also carries "decode_batch" (one GPU): the four projection shapes
+at M in {1, 4, 8, 16}, one launch at a time; and "sharded_70b": Llama-3-70B layer projections
 column-sharded over the same N GPUs at M in {1, 16, 256, 4096} (see
 sharded_70b).
 
@@ -262,6 +263,44 @@ def int3_and_dequant(dev):
             byts = words * (4 + 2 + 2 + 2 * per_word)
         us = _graph_us(dev, calls)
         out["dequant"][kind] = {"words": words, "us": round(us, 3), "GB/s": round(byts / us / 1e3, 1)}
+        del Ws
+    return out
+
+
+def decode_batch(dev, Ms=(1, 4, 8, 16), reps=10):
+    """The decode skinny-GEMM configuration in full: the four Llama-3-8B
+    projection shapes at M in {1, 4, 8, 16} through the public op, each a CUDA
+    graph over a pool of distinct weights >= 4x L2, CUDA events; GB/s of
+    algorithmic bytes per launch."""
+    from t4_cuda_b200 import ops
+    gen = torch.Generator(device=dev).manual_seed(1)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    out = {}
+    for K, N in ((4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)):
+        pool = max(2, math.ceil(4 * l2 / (K * N // 2)))
+        Ws = [torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=gen)
+              for _ in range(pool)]
+        S = (torch.randn((K // GROUP, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+        row = {}
+        for M in Ms:
+            A = torch.randn((M, K), device=dev, generator=gen).half()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for W in Ws:
+                    ops.fused_w4a16_gemm_s4(A, W, S, None)
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * pool)
+            row[f"M={M}"] = {"us": round(us, 3), "GB/s": round(alg_bytes(M, K, N) / us / 1e3, 1)}
+            del g
+        out[f"{K}x{N}"] = row
         del Ws
     return out
 
@@ -522,6 +561,7 @@ def run_ours(args):
     others = None
     if world == 1 and not args.no_gemm:
         others = int3_and_dequant(dev)
+    batch = decode_batch(dev) if world == 1 else None
 
     # ---- end to end through the public API, host buffers, copies timed
     pin = {a: t.cpu().pin_memory() for a, t in acts.items()}
@@ -636,6 +676,8 @@ def run_ours(args):
         line["gemm"] = gemm
     if others is not None:
         line["other_kernels"] = others
+    if batch is not None:
+        line["decode_batch"] = batch
     if sh70 is not None:
         line["sharded_70b"] = sh70
     if world == 1 and not args.no_cpu_baseline:

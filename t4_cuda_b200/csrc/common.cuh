@@ -30,7 +30,8 @@ int sm_count();
 int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
                    int K, int group, cudaStream_t stream);
 
-// Decode GEMV with resident activations (M <= 16, M * K <= 32768); returns
+// Decode GEMV with resident activations (M <= 16; M * K <= 32768, or larger
+// when the activations still fit in shared memory and N / 16 >= SMs); returns
 // T4B_ERR_UNSUPPORTED (without launching) for shapes it does not take.
 int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
                    int K, int group, cudaStream_t stream);

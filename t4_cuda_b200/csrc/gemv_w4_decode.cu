@@ -2,7 +2,9 @@
 //
 //   C[M, N] = A[M, K] x dequant(W)[K, N],  W int32 [K/8, N], group scales [K/g, N]
 //
-// for M <= 16 and M * K <= 32768 (one token, or a handful, per call).
+// for M <= 16 (one token, or a handful, per call) whose activations fit in
+// shared memory next to a ring of at least two stages; past M * K = 32768 only
+// for shapes with at least one 16-column tile per SM.
 //
 // Work decomposition
 //   Output columns are cut into 16-column tiles.  CTA b of G (G <= SMs) owns
@@ -858,7 +860,7 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
                        bool plan_only = false) {
     const int KW = K / 8;
     const int gw = group / 8;
-    if (M > 16 || (long long)M * K > 32768) return T4B_ERR_UNSUPPORTED;
+    if (M > 16) return T4B_ERR_UNSUPPORTED;
     if ((K % 128) != 0 || (N % 8) != 0) return T4B_ERR_UNSUPPORTED;
     if (!aligned(A, 16) || !aligned(W, 16) || !aligned(S, 16) || (Z && !aligned(Z, 16))) return T4B_ERR_UNSUPPORTED;
     const int MT = (M <= 8) ? 1 : 2;
@@ -877,6 +879,10 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
     p.KWp = (KW + pad_rows - 1) / pad_rows * pad_rows;
     p.T = (N + kBoxCols - 1) / kBoxCols;
     p.G = p.T < sm_count() ? p.T : sm_count();
+    // Every CTA stages all of A (M * K * 2 bytes).  Past M * K = 32768 that
+    // only pays when each SM has at least one whole column tile to spend it
+    // on; narrower shapes go to the K-split stream kernel.
+    if ((long long)M * K > 32768 && p.T < sm_count()) return T4B_ERR_UNSUPPORTED;
     if ((long long)p.T * p.G >= (1ll << 32)) return T4B_ERR_UNSUPPORTED;
     p.gw = gw;
     p.gw_shift = -1;

@@ -79,6 +79,9 @@ SHAPES = [
     (1, 1024, 9600, 128, None),      # 4-5 tiles per CTA (a lone last tile)
     (3, 256, 7904, 128, "int"),      # 3-4 tiles per CTA (three-tile groups)
     (4, 1024, 512, 32, None),        # group 32: not the decode kernel's (falls back)
+    (16, 4096, 2400, 128, "int"),    # M * K > 32768 with >= 148 column tiles: decode kernel, 4 ring stages
+    (4, 14336, 2384, 128, "frac"),   # same at K = 14336 (57 KB of activations per batch row pair)
+    (16, 4096, 1024, 128, None),     # M * K > 32768 with 64 tiles: the stream kernel's K split
 ]
 
 

@@ -752,30 +752,60 @@ def run_reference(args):
 
 def run_case(spec, launches=6):
     """Profiling driver (no JSON line): a few launches of ONE kernel on one
-    case, for ncu captures of a single kernel.
-      decode:K:N:M  s4 group-128 GEMV/skinny GEMM, weights rotating through a
-                    pool of >= 4x L2 so every launch reads them from HBM
-      gemm:M:K:N    s4 group-128 prefill GEMM (tcgen05)"""
+    case, for ncu captures of a single kernel.  Weights rotate through a pool
+    of >= 4x L2 (except gemm), so every launch reads them from HBM.
+      decode:K:N:M   s4 group-128 GEMV / skinny GEMM (default dispatch)
+      stream:K:N:M   the same through the split-tile stream kernel
+      gemm:M:K:N     s4 group-128 prefill GEMM (tcgen05)
+      int3:K:N       H17 INT3 GEMV, M = 1, group 128 (K a multiple of 10)
+      dequant:KIND:W flat dequant (KIND s4, s3 or fp8; magic mode) of W words"""
     from t4_cuda_b200 import ops
     kind, *dims = spec.split(":")
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     gen = torch.Generator(device=dev).manual_seed(5)
-    if kind == "decode":
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+
+    def pool_of(nbytes, make):
+        return [make() for _ in range(max(4, (4 * l2) // nbytes + 1))]
+
+    if kind in ("decode", "stream"):
         K, N, M = (int(x) for x in dims)
-        l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-        pool = max(4, (4 * l2) // (K * N // 2) + 1)
-        Ws = [torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=gen)
-              for _ in range(pool)]
+        Ws = pool_of(K * N // 2, lambda: torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32,
+                                                         device=dev, generator=gen))
     elif kind == "gemm":
         M, K, N = (int(x) for x in dims)
         Ws = [torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=gen)]
+    elif kind == "int3":
+        K, N = (int(x) for x in dims)
+        Ws = pool_of((K // 10) * N * 4, lambda: torch.randint(0, 2 ** 30, (K // 10, N), dtype=torch.int32,
+                                                                device=dev, generator=gen))
+        S = (torch.randn((-(-K // 128), N), device=dev, generator=gen).abs() * 0.02).half()
+        A = torch.randn((1, K), device=dev, generator=gen).half()
+        Z = torch.empty(0, dtype=torch.float16, device=dev)
+        for i in range(launches):
+            C = ops.fused_h17_gemv_s3(A, Ws[i % len(Ws)], S, Z, group_size=128)
+    elif kind == "dequant":
+        dk, words = dims[0], int(dims[1])
+        per = {"s4": 8, "s3": 10, "fp8": 4}[dk]
+        Ws = pool_of(words * (8 + 2 * per), lambda: torch.randint(0, 2 ** 30, (words,), dtype=torch.int32,
+                                                                    device=dev, generator=gen))
+        S = (torch.randn(words, device=dev, generator=gen) * 0.02).half()
+        Zp = torch.zeros(words, device=dev, dtype=torch.float16)
+        for i in range(launches):
+            W = Ws[i % len(Ws)]
+            C = (ops.dequantize_fp8(W, S, mode="magic") if dk == "fp8" else
+                 getattr(ops, f"dequantize_{dk}")(W, S, Zp, mode="magic"))
     else:
         raise SystemExit(f"unknown case {spec!r}")
-    S = (torch.randn((K // GROUP, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
-    A = torch.randn((M, K), device=dev, generator=gen).half()
-    for i in range(launches):
-        C = ops.fused_w4a16_gemm_s4(A, Ws[i % len(Ws)], S, None)
+    if kind in ("decode", "stream", "gemm"):
+        S = (torch.randn((K // GROUP, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+        A = torch.randn((M, K), device=dev, generator=gen).half()
+        prev = ops.set_gemv_kernel("stream") if kind == "stream" else None
+        for i in range(launches):
+            C = ops.fused_w4a16_gemm_s4(A, Ws[i % len(Ws)], S, None)
+        if prev is not None:
+            ops.set_gemv_kernel(prev)
     torch.cuda.synchronize()
     err = ops.device_error(dev)
     print(f"case {spec}: {launches} launches, mean |C| {float(C.float().abs().mean()):.4f}, device error {err}")
@@ -795,11 +825,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nccl-gather", action="store_true", help="N > 1: NCCL all-gather instead of the fused one")
     ap.add_argument("--no-70b", action="store_true", help="skip the column-sharded Llama-3-70B layer section")
-    ap.add_argument("--case", help="profiling driver: decode:K:N:M or gemm:M:K:N (a few launches, no JSON)")
+    ap.add_argument("--case", help="profiling driver, comma-separated cases (see run_case; a few launches, no JSON)")
     ap.add_argument("--launches", type=int, default=6, help="launches for --case")
     args = ap.parse_args()
     if args.case:
-        run_case(args.case, args.launches)
+        for spec in args.case.split(","):
+            run_case(spec, args.launches)
+            torch.cuda.empty_cache()
         return
     args.warmup = max(3, args.warmup)     # at least 3 untimed warm-up steps
     if args.impl == "reference":

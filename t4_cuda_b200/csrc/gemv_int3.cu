@@ -27,6 +27,13 @@ constexpr int kWarps = 8;
 constexpr int kTileN = 64;
 constexpr int kNB = 2;
 
+// CTAs per SM the register budget is sized for.  The kernel is latency-bound
+// (a warp's dequant + MMA chain per step), so warps per SM matter more than
+// registers: the M <= 8, no-zero-point form fits two CTAs (128 registers, a
+// few bytes of spill); the others need ~170-240 registers and stay at one.
+template <int MT, bool HAS_ZP>
+constexpr int min_blocks() { return (MT == 1 && !HAS_ZP) ? 2 : 1; }
+
 struct Int3Params {
     const uint16_t* A;       // [M, K]
     const uint32_t* W;       // [K/10, N]
@@ -219,7 +226,7 @@ __device__ __forceinline__ void compute_step(const Int3Step<MT, HAS_ZP>& d, floa
 }
 
 template <int MT, bool HAS_ZP, bool VEC, bool CLUSTER>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, min_blocks<MT, HAS_ZP>())
 gemv_int3_kernel(const Int3Params p) {
     constexpr int MR = 8 * MT;
     constexpr int RED_STRIDE = MR + 1;
@@ -356,10 +363,10 @@ int fused_int3(const void* A, const void* W, const void* S, const void* Z, void*
     const int mt = (M <= 8) ? 1 : 2;
     const int tiles = (N + kTileN - 1) / kTileN;
     const int chunks = (M + 8 * mt - 1) / (8 * mt);
-    // One CTA per SM fits (the kernel holds ~140 registers per thread), so
-    // split K only as far as one wave of CTAs covers the SMs: a second wave
-    // would repeat the whole load round trip.
-    int splits = sm_count() / (tiles * chunks);
+    // Split K only as far as one wave of CTAs covers the SMs (min_blocks per
+    // SM): a second wave would repeat the whole load round trip.
+    const int per_sm = (mt == 1 && !Z) ? min_blocks<1, false>() : 1;
+    int splits = per_sm * sm_count() / (tiles * chunks);
     if (splits > 8) splits = 8;
     while (splits > 1 && splits * kWarps > p.total_steps) --splits;
     if (splits < 1) splits = 1;

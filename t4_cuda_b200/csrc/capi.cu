@@ -61,17 +61,38 @@ int acquire_workspace(cudaStream_t stream, size_t counter_words, size_t part_flo
         cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
         e = cudaStreamIsCapturing(stream, &cap);
         if (e != cudaSuccess) return record_cuda_error(e);
-        if (cap != cudaStreamCaptureStatusNone) return T4B_ERR_UNSUPPORTED;
+        const bool capturing = cap != cudaStreamCaptureStatusNone;
         // Grow with headroom; the previous buffer may still be in use by queued
-        // kernels, so it is kept (not freed) -- growth is rare and bounded.
+        // kernels (or by a captured graph), so it is kept, never freed --
+        // growth is rare and bounded.
         const size_t cw = round_up(std::max(counter_words * 2, std::max(buf.counter_words, (size_t)65536)), 64);
         const size_t pf = round_up(std::max(part_floats * 2, std::max(buf.part_floats, (size_t)(1 << 20))), 64);
         const size_t bytes = kHeaderBytes + cw * 4 + pf * 4;
         void* p = nullptr;
-        e = cudaMalloc(&p, bytes);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        e = cudaMemsetAsync(p, 0, kHeaderBytes + cw * 4, stream);
-        if (e != cudaSuccess) return record_cuda_error(e);
+        if (capturing) {
+            // First use on a stream that is being captured into a CUDA graph
+            // (torch captures on a side stream of its own).  A cudaMalloc is
+            // allowed during capture once this thread's capture mode is
+            // relaxed; the buffer is zeroed on a private stream and waited for
+            // here, outside the graph, and it is never freed, so the graph's
+            // kernels can rely on it at every replay.
+            cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+            e = cudaThreadExchangeStreamCaptureMode(&mode);
+            if (e != cudaSuccess) return record_cuda_error(e);
+            cudaStream_t zs = nullptr;
+            e = cudaMalloc(&p, bytes);
+            if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&zs, cudaStreamNonBlocking);
+            if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, kHeaderBytes + cw * 4, zs);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(zs);
+            if (zs) cudaStreamDestroy(zs);
+            cudaThreadExchangeStreamCaptureMode(&mode);      // back to the caller's mode
+            if (e != cudaSuccess) return record_cuda_error(e);
+        } else {
+            e = cudaMalloc(&p, bytes);
+            if (e != cudaSuccess) return record_cuda_error(e);
+            e = cudaMemsetAsync(p, 0, kHeaderBytes + cw * 4, stream);
+            if (e != cudaSuccess) return record_cuda_error(e);
+        }
         buf.base = p;
         buf.counter_words = cw;
         buf.part_floats = pf;

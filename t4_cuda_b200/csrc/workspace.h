@@ -17,9 +17,9 @@ struct Workspace {
 // counters and `part_floats` partial sums.  One buffer per (device, stream):
 // kernels queued on the same stream run in order, so they can share it.  The
 // buffer is allocated (cudaMalloc) and zeroed on the first request and grown
-// when a request is larger; allocation is refused while the stream is being
-// captured into a CUDA graph (T4B_ERR_UNSUPPORTED) -- make one call of the
-// same or a larger shape before capturing.
+// when a request is larger, also while the stream is being captured into a
+// CUDA graph (the allocation then happens at capture time, outside the graph);
+// buffers are never freed.
 int acquire_workspace(cudaStream_t stream, size_t counter_words, size_t part_floats, Workspace* ws);
 
 }  // namespace t4b

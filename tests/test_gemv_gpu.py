@@ -194,3 +194,25 @@ def test_bad_shapes_raise(cuda_device):
         t4_kernels.fused_w4a16_gemm_u4(A, W, torch.ones(3, 16, dtype=torch.float16, device=cuda_device), None)
     with pytest.raises(RuntimeError):
         t4_kernels.fused_w4a16_gemm_u4(A, W, s[:, :8], None)             # scale columns != N
+
+
+def test_stream_kernel_inside_graph_capture(cuda_device):
+    """A shape only the split-tile stream kernel takes (M * K too large for the
+    decode kernel's resident activations, fewer tiles than SMs), first called
+    while a brand-new stream is being captured: the kernel's workspace is made
+    at capture time, and every replay equals the eager result bit for bit (the
+    stream kernel reduces its split tiles in a fixed order)."""
+    rng = np.random.default_rng(33)
+    A, W, s, z, At, Wt, st, zt = make_case(rng, 16, 8192, 512, 128, None, cuda_device)
+    eager = t4_kernels.fused_w4a16_gemm_s4(At, Wt, st, None)
+    ref = oracle.ref_w4_gemm(A, W, s, None, signed=True)
+    assert_gemm_close(eager, ref, "s4")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=torch.cuda.Stream(cuda_device)):
+        out = t4_kernels.fused_w4a16_gemm_s4(At, Wt, st, None)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    assert t4_cuda_b200.device_error(cuda_device) == 0

@@ -161,15 +161,12 @@ __device__ __forceinline__ void load_step(const Int3Params& p, Int3Step<MT, HAS_
     }
 }
 
-// PRMT selectors for element pair (i, i+5) of a word whose elements from
-// `split` on use the next group: output half 0 takes element i's scale, half
-// 1 element (i+5)'s, each from the low pair (bytes 0-3: this group) or the
-// high pair (bytes 4-7: the next group).  These select slot 0 of the pair;
-// slot 1 (the pair's upper half) adds 0x2222.  split = 10: no straddle.
-__device__ __forceinline__ uint32_t pair_selector(int i, int split) {
-    const uint32_t x0 = (i >= split) ? 4u : 0u;
-    const uint32_t x1 = (i + 5 >= split) ? 4u : 0u;
-    return x0 | ((x0 + 1u) << 4) | (x1 << 8) | ((x1 + 1u) << 12);
+// Scale (and zero-point) pair for element pair (i, i+5) of slot j when the word
+// straddles: element x uses the next group iff x >= split.
+__device__ __forceinline__ uint32_t pick_pair(uint32_t lo_pair2, uint32_t hi_pair2, int j, int i, int split) {
+    const uint16_t lo = (j & 1) ? (uint16_t)(lo_pair2 >> 16) : (uint16_t)(lo_pair2 & 0xFFFF);
+    const uint16_t hi = (j & 1) ? (uint16_t)(hi_pair2 >> 16) : (uint16_t)(hi_pair2 & 0xFFFF);
+    return h2_pack(i >= split ? hi : lo, (i + 5) >= split ? hi : lo);
 }
 
 template <int MT, bool HAS_ZP>
@@ -187,26 +184,17 @@ __device__ __forceinline__ void compute_step(const Int3Step<MT, HAS_ZP>& d, floa
             b[mt][5 * e + 3] = prmt(x[1], x[4], 0x5432);
             b[mt][5 * e + 4] = prmt(x[2], x[4], 0x7610);
         }
-    // A word that straddles a group boundary (group 128: about half of the
-    // 8-row steps hold one) needs a scale per element.  The choice is made
-    // per warp, so a warp never runs both paths: when any lane straddles, every
-    // lane picks its scales with one PRMT per element pair (a lane without a
-    // straddle selects its own group throughout).
-    bool uniform[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) uniform[e] = __all_sync(0xffffffffu, d.split[e] >= 10);
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         uint32_t Q[2][10];   // [row r / r+8][5 e + i]
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
             const int j = 2 * t + rr;
-            const uint32_t hsel = (j & 1) ? 0x2222u : 0u;
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 uint32_t q[5];
                 unpack_s3_exact(d.w[e][j], q);
-                if (uniform[e]) {
+                if (d.split[e] >= 10) {
                     const uint32_t sp = d.slo[e][j >> 1];
                     const uint32_t s2 = prmt(sp, sp, (j & 1) ? 0x3232 : 0x1010);
                     uint32_t z2 = 0;
@@ -219,10 +207,10 @@ __device__ __forceinline__ void compute_step(const Int3Step<MT, HAS_ZP>& d, floa
                 } else {
 #pragma unroll
                     for (int i = 0; i < 5; ++i) {
-                        const uint32_t sel = pair_selector(i, d.split[e]) + hsel;
-                        const uint32_t s2 = prmt(d.slo[e][j >> 1], d.shi[e][j >> 1], sel);
+                        const uint32_t s2 = pick_pair(d.slo[e][j >> 1], d.shi[e][j >> 1], j, i, d.split[e]);
                         uint32_t qi = q[i];
-                        if constexpr (HAS_ZP) qi = h2_sub(qi, prmt(d.zlo[e][j >> 1], d.zhi[e][j >> 1], sel));
+                        if constexpr (HAS_ZP)
+                            qi = h2_sub(qi, pick_pair(d.zlo[e][j >> 1], d.zhi[e][j >> 1], j, i, d.split[e]));
                         Q[rr][5 * e + i] = h2_mul(qi, s2);
                     }
                 }

@@ -1,6 +1,6 @@
-"""The fused GEMV + all-gather on two GPUs (skipped with fewer): two ranks
-(processes; NCCL only to exchange the receive buffers' handles) each hold half
-the columns of the projections of two groups -- three projections at M = 1
+"""The fused GEMV + all-gather on two and four GPUs (each case skipped with
+fewer): the ranks (processes; NCCL only to exchange the receive buffers'
+handles) each hold their share of the columns of the projections of two groups -- three projections at M = 1
 and one at M = 3 -- and call them in the order G1, G2, G1, G2, G1 with fresh
 activations each time.  After every call each rank's outputs hold the whole
 projection outputs, equal to the oracle within the GEMV gate, and the device
@@ -72,13 +72,16 @@ def _worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_allgather_two_ranks(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_fused_allgather_ranks(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import oracle
     import torch.multiprocessing as mp
-    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
     weights = [_weights(0, G1[1]), _weights(1, G2[1])]
-    for rank in range(2):
+    for rank in range(world):
         d = np.load(os.path.join(tmp_path, f"rank{rank}.npz"))
         assert int(d["err"]) == 0
         for c, gi in enumerate(CALLS):

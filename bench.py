@@ -18,7 +18,8 @@ column-sharded N ways and the outputs are gathered by the decode kernel itself
 uses NCCL all-gather instead): the same token, so "scaling" is "strong".
 
 The line also carries "decode_batch" (one GPU): the four projection shapes
-at M in {1, 4, 8, 16}, one launch at a time; and "sharded_70b": Llama-3-70B layer projections
+at M in {1, 4, 8, 16}, one launch at a time; "gemm_sweep" (one GPU): the
+same shapes at M in {512, 2048, 4096} on the tcgen05 GEMM; and "sharded_70b": Llama-3-70B layer projections
 column-sharded over the same N GPUs at M in {1, 16, 256, 4096} (see
 sharded_70b).
 
@@ -264,6 +265,35 @@ def int3_and_dequant(dev):
         us = _graph_us(dev, calls)
         out["dequant"][kind] = {"words": words, "us": round(us, 3), "GB/s": round(byts / us / 1e3, 1)}
         del Ws
+    return out
+
+
+def gemm_sweep(dev, Ms=(512, 2048, 4096), reps=5):
+    """The prefill configuration in full: the four Llama-3-8B projection shapes
+    at M in {512, 2048, 4096} through the public op (tcgen05 GEMM), CUDA
+    events around `reps` launches; TFLOP/s = 2 M K N / time."""
+    from t4_cuda_b200 import ops
+    gen = torch.Generator(device=dev).manual_seed(12)
+    out = {}
+    for K, N in ((4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)):
+        W = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=gen)
+        S = (torch.randn((K // GROUP, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+        row = {}
+        for M in Ms:
+            A = torch.randn((M, K), device=dev, generator=gen).half()
+            for _ in range(2):
+                ops.fused_w4a16_gemm_s4(A, W, S, None)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                ops.fused_w4a16_gemm_s4(A, W, S, None)
+            e1.record()
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            row[f"M={M}"] = {"us": round(us, 2), "TFLOP/s": round(2.0 * M * K * N / us / 1e6, 1)}
+        out[f"{K}x{N}"] = row
+        del W
     return out
 
 
@@ -562,6 +592,7 @@ def run_ours(args):
     if world == 1 and not args.no_gemm:
         others = int3_and_dequant(dev)
     batch = decode_batch(dev) if world == 1 else None
+    sweep = gemm_sweep(dev) if world == 1 and not args.no_gemm else None
 
     # ---- end to end through the public API, host buffers, copies timed
     pin = {a: t.cpu().pin_memory() for a, t in acts.items()}
@@ -678,6 +709,8 @@ def run_ours(args):
         line["other_kernels"] = others
     if batch is not None:
         line["decode_batch"] = batch
+    if sweep is not None:
+        line["gemm_sweep"] = sweep
     if sh70 is not None:
         line["sharded_70b"] = sh70
     if world == 1 and not args.no_cpu_baseline:

@@ -29,6 +29,7 @@
 // error word, stops the pipeline and still frees TMEM before the CTA exits.
 #include "common.cuh"
 #include "tma.cuh"
+#include "workspace.h"
 
 namespace t4b {
 namespace {
@@ -56,7 +57,15 @@ struct GemmParams {
     int M, N, K;
     int gw_steps;       // K steps (of 64) per scale group (0: a single group, per-column scales)
     int ksteps;
+    // split K (single-CTA kernel): blockIdx.z takes K steps [z * ks_per, ...);
+    // each CTA stores its fp32 tile to part, and the last of a tile's CTAs
+    // (counter) sums the ksplit partials in split order and writes C
+    int ksplit, ks_per;
+    float* part;            // [tiles][ksplit][128][256]
+    unsigned* counters;     // one per tile, zero between launches
 };
+
+constexpr int kMinSplitSteps = 8;       // K steps (512 K) a split takes at least
 
 struct GemmMaps {
     CUtensorMap a;      // A [M, K] fp16, box 64 x 128, 128-byte swizzle
@@ -157,6 +166,9 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+    const int k_begin = blockIdx.z * p.ks_per;
+    const int nsteps = min(p.ks_per, p.ksteps - k_begin);   // >= 1: the host sizes the split so
+    volatile int* last_flag = abort_flag + 1;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTmaStages; ++s) {
@@ -188,15 +200,16 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     if (warp == 0) {
         // ---------------- TMA producer
         if (lane == 0) {
-            for (int i = 0; i < p.ksteps; ++i) {
+            for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kTmaStages;
                 const uint32_t ph = (uint32_t)((i / kTmaStages) & 1);
                 if (i >= kTmaStages && !wait_or_abort(&empty_tma[s], ph ^ 1u, abort_flag)) break;
                 uint8_t* st = base + s * kTmaStageBytes;
-                const int srow = p.gw_steps ? i / p.gw_steps : 0;
+                const int kg = k_begin + i;                         // K step in the whole of K
+                const int srow = p.gw_steps ? kg / p.gw_steps : 0;
                 mbar_arrive_expect_tx(&full_tma[s], kABytes + kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
-                tma_load_2d(st, &maps.a, i * kBK, m0, &full_tma[s]);
-                tma_load_2d(st + kABytes, &maps.w, n0, i * (kBK / 8), &full_tma[s]);
+                tma_load_2d(st, &maps.a, kg * kBK, m0, &full_tma[s]);
+                tma_load_2d(st + kABytes, &maps.w, n0, kg * (kBK / 8), &full_tma[s]);
                 tma_load_2d(st + kABytes + kWBytes, &maps.s, n0, srow, &full_tma[s]);
                 if constexpr (HAS_ZP)
                     tma_load_2d(st + kABytes + kWBytes + kSBytes, &maps.z, n0, srow, &full_tma[s]);
@@ -208,13 +221,13 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
             // The dequant warps arrive on full_b[b] only after waiting for the
             // stage's TMA copy, so full_b alone certifies both operands.
             bool ready = mbar_try_wait(&full_b[0], 0);
-            for (int i = 0; i < p.ksteps; ++i) {
+            for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kTmaStages, b = i % kBStages;
                 if (!ready && !wait_or_abort(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag)) break;
                 // peek at the next stage while this one's MMAs queue (no tcgen05 fence
                 // per stage: the barrier orders the operands, and a fence here would
                 // hold the issuer until the queued MMAs drain)
-                ready = (i + 1 < p.ksteps) &&
+                ready = (i + 1 < nsteps) &&
                         mbar_try_wait(&full_b[(i + 1) % kBStages], (uint32_t)(((i + 1) / kBStages) & 1));
                 const uint32_t a_addr = smem_addr(base + s * kTmaStageBytes);
                 const uint32_t b_addr = smem_addr(bring + b * kBBytes);
@@ -231,7 +244,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         // ---------------- dequant warpgroups (warps 2..17), then epilogue
         const int n = (threadIdx.x - 64) & (kBN - 1);       // column of the tile
         const int j0 = ((threadIdx.x - 64) >> 8) * 4;       // word rows j0 .. j0 + 3 of the K step
-        for (int i = 0; i < p.ksteps; ++i) {
+        for (int i = 0; i < nsteps; ++i) {
             const int s = i % kTmaStages, b = i % kBStages;
             if (!wait_or_abort(&full_tma[s], (uint32_t)((i / kTmaStages) & 1), abort_flag)) break;
             if (i >= kBStages && !wait_or_abort(&empty_b[b], (uint32_t)(((i / kBStages) & 1) ^ 1), abort_flag)) break;
@@ -275,10 +288,65 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         const int quarter = warp & 3;                       // TMEM lanes this warp may read
         const int cq = (warp - 2) >> 2;                     // which 64 columns
         const int row = m0 + 32 * quarter + lane;
-        if (ok) {
+        bool store = ok;
+        if (p.ksplit > 1) {
+            // Split K: this CTA's fp32 tile goes to its partial slot; the last
+            // CTA of the tile to arrive adds the ksplit partials in split order
+            // (its own from TMEM) -- the same sum whichever CTA is last.  Every
+            // dequant warp reaches both barriers (ok may differ per thread after
+            // a timeout), and every CTA counts its arrival, so the counter is
+            // back at zero when the launch ends even after an abort (whose
+            // output is then wrong, and flagged in the error word).
+            const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+            const int r = 32 * quarter + lane;
+            float* mine = p.part + (((size_t)tile * p.ksplit + blockIdx.z) * kBM + r) * kBN;
+            if (ok) {
+                for (int c0 = 64 * cq; c0 < 64 * cq + 64; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+#pragma unroll
+                    for (int k = 0; k < 32; k += 4)
+                        __stcg(reinterpret_cast<float4*>(mine + c0 + k),
+                               make_float4(__uint_as_float(v[k]), __uint_as_float(v[k + 1]),
+                                           __uint_as_float(v[k + 2]), __uint_as_float(v[k + 3])));
+                }
+            }
+            __threadfence();
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * kDqWarps) : "memory");
+            if (threadIdx.x == 64) {
+                const bool last = atomicAdd(p.counters + tile, 1u) == (unsigned)(p.ksplit - 1);
+                if (last) p.counters[tile] = 0u;     // every CTA of the tile has arrived
+                *last_flag = last ? 1 : 0;
+                __threadfence();
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * kDqWarps) : "memory");
+            store = ok && *last_flag != 0;
+        }
+        if (store) {
             for (int c0 = 64 * cq; c0 < 64 * cq + 64; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+                if (p.ksplit > 1) {
+                    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+                    const int r = 32 * quarter + lane;
+                    const float* src = p.part + ((size_t)tile * p.ksplit * kBM + r) * kBN + c0;
+                    const size_t zstride = (size_t)kBM * kBN;
+#pragma unroll
+                    for (int k = 0; k < 32; k += 4) {
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int z = 0; z < p.ksplit; ++z) {
+                            const float4 f = (z == (int)blockIdx.z)
+                                ? make_float4(__uint_as_float(v[k]), __uint_as_float(v[k + 1]),
+                                              __uint_as_float(v[k + 2]), __uint_as_float(v[k + 3]))
+                                : __ldcg(reinterpret_cast<const float4*>(src + z * zstride + k));
+                            acc.x += f.x; acc.y += f.y; acc.z += f.z; acc.w += f.w;
+                        }
+                        v[k] = __float_as_uint(acc.x);
+                        v[k + 1] = __float_as_uint(acc.y);
+                        v[k + 2] = __float_as_uint(acc.z);
+                        v[k + 3] = __float_as_uint(acc.w);
+                    }
+                }
                 if (row < p.M) {
                     uint16_t* crow = p.C + (size_t)row * p.N + n0 + c0;
                     if (n0 + c0 + 32 <= p.N) {
@@ -649,7 +717,7 @@ int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
         if (e != cudaSuccess) return record_cuda_error(e);
         configured = true;
     }
-    dim3 grid((p.N + kBN - 1) / kBN, (p.M + kBM - 1) / kBM, 1);
+    dim3 grid((p.N + kBN - 1) / kBN, (p.M + kBM - 1) / kBM, p.ksplit);
     kern<<<grid, kThreads, smem, stream>>>(maps, p);
     return check_launch();
 }
@@ -675,8 +743,30 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
     p.M = M; p.N = N; p.K = K;
     p.ksteps = K / kBK;
     p.gw_steps = (group >= K) ? 0 : group / kBK;
-    // M > 128: CTA pairs (each CTA dequantizes 128 of a pair's 256 columns)
-    const bool use_pair = M > kBM && allow_pairs;
+    p.ksplit = 1;
+    p.ks_per = p.ksteps;
+    p.part = nullptr;
+    p.counters = nullptr;
+    // M > 128: CTA pairs (each CTA dequantizes 128 of a pair's 256 columns) --
+    // unless the tiles leave SMs idle: then single-CTA tiles with K split
+    // across CTAs until about one CTA per SM (at least 8 K steps a split).
+    bool use_pair = M > kBM && allow_pairs;
+    const int sms = sm_count();
+    const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    const int pair_ctas = 2 * ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
+    if (tiles < sms && (!use_pair || pair_ctas < sms)) {
+        int ks = std::min(std::min(sms / tiles, p.ksteps / kMinSplitSteps), 8);
+        if (ks >= 2) {
+            p.ks_per = (p.ksteps + ks - 1) / ks;
+            p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;      // no empty split
+            Workspace ws;
+            const int st = acquire_workspace(stream, (size_t)tiles, (size_t)tiles * p.ksplit * kBM * kBN, &ws);
+            if (st != T4B_OK) return st;
+            p.part = ws.part;
+            p.counters = ws.counters;
+            use_pair = false;
+        }
+    }
     const uint32_t wbox = use_pair ? pair::kHalf : kBN;
     GemmMaps maps;
     if (!make_tmap_2d_ex(&maps.a, true, A, (uint64_t)M, (uint64_t)K, kBM, kBK, 128, 256) ||

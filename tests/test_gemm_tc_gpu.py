@@ -31,7 +31,8 @@ SHAPES = [
     (1000, 1024, 4096, 128, "int"),    # ragged M
     (257, 512, 512, 64, "int"),        # second pair holds one valid row
     (129, 1024, 264, 128, None),       # smallest M on pairs; N tail of 8 columns
-    (2048, 4096, 1024, 128, None),
+    (2048, 4096, 1024, 128, None),     # 64 tiles: K split in two
+    (128, 1472, 512, 64, "frac"),      # 23 K steps split 12 + 11
 ]
 
 
@@ -74,9 +75,10 @@ def test_tc_gemm_matches_generic_kernel(cuda_device):
 
 def test_pair_and_single_cta_kernels_agree(cuda_device):
     """Both tensor-core kernels accumulate each output in fp32 over K in the
-    same 16-wide steps; their results agree far inside the gate."""
+    same 16-wide steps; their results agree far inside the gate.  (A shape
+    with enough tiles that neither splits K.)"""
     rng = np.random.default_rng(8)
-    A, W, s, z, At, Wt, st, zt = make_case(rng, 640, 2048, 1536, 128, "int", cuda_device)
+    A, W, s, z, At, Wt, st, zt = make_case(rng, 640, 2048, 8192, 128, "int", cuda_device)
     prev = t4_cuda_b200.set_gemv_kernel("tc_single")
     try:
         C1 = t4_kernels.fused_w4a16_gemm_u4(At, Wt, st, zt)
@@ -87,3 +89,19 @@ def test_pair_and_single_cta_kernels_agree(cuda_device):
     assert t4_cuda_b200.device_error(cuda_device) == 0
     d = (C1.float() - C2.float()).abs().max().item()
     assert d <= 1e-3 * C1.float().abs().max().item()
+
+
+def test_split_k_matches_unsplit(cuda_device):
+    """A shape with few tiles splits K across CTAs (partials summed in split
+    order by the tile's last CTA); it agrees with the same product computed
+    unsplit, as extra rows of a larger M, far inside the gate."""
+    rng = np.random.default_rng(9)
+    A, W, s, z, At, Wt, st, zt = make_case(rng, 256, 4096, 1024, 128, None, cuda_device)
+    C = t4_kernels.fused_w4a16_gemm_s4(At, Wt, st, None)               # 8 tiles: K split 8 ways
+    big = torch.cat([At] * 20)                                          # 5120 rows: 160 tiles, no split
+    Cb = t4_kernels.fused_w4a16_gemm_s4(big, Wt, st, None)
+    torch.cuda.synchronize(cuda_device)
+    assert t4_cuda_b200.device_error(cuda_device) == 0
+    d = (C.float() - Cb[:256].float()).abs().max().item()
+    assert d <= 1e-3 * Cb.float().abs().max().item()
+    assert torch.equal(C, t4_kernels.fused_w4a16_gemm_s4(At, Wt, st, None))   # deterministic

@@ -270,8 +270,9 @@ def int3_and_dequant(dev):
 
 def gemm_sweep(dev, Ms=(512, 2048, 4096), reps=5):
     """The prefill configuration in full: the four Llama-3-8B projection shapes
-    at M in {512, 2048, 4096} through the public op (tcgen05 GEMM), CUDA
-    events around `reps` launches; TFLOP/s = 2 M K N / time."""
+    at M in {512, 2048, 4096} through the public op (tcgen05 GEMM), a CUDA
+    graph of `reps` launches timed with CUDA events (short kernels launched
+    one by one from Python would measure the host); TFLOP/s = 2 M K N / time."""
     from t4_cuda_b200 import ops
     gen = torch.Generator(device=dev).manual_seed(12)
     out = {}
@@ -281,16 +282,7 @@ def gemm_sweep(dev, Ms=(512, 2048, 4096), reps=5):
         row = {}
         for M in Ms:
             A = torch.randn((M, K), device=dev, generator=gen).half()
-            for _ in range(2):
-                ops.fused_w4a16_gemm_s4(A, W, S, None)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(reps):
-                ops.fused_w4a16_gemm_s4(A, W, S, None)
-            e1.record()
-            e1.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / reps
+            us = _graph_us(dev, [lambda: ops.fused_w4a16_gemm_s4(A, W, S, None)] * reps, reps=4)
             row[f"M={M}"] = {"us": round(us, 2), "TFLOP/s": round(2.0 * M * K * N / us / 1e6, 1)}
         out[f"{K}x{N}"] = row
         del W

@@ -66,6 +66,7 @@ struct GemmParams {
 };
 
 constexpr int kMinSplitSteps = 8;       // K steps (512 K) a split takes at least
+constexpr int kMinSplitK = 8192;        // K below which the GEMM never splits K
 
 struct GemmMaps {
     CUtensorMap a;      // A [M, K] fp16, box 64 x 128, 128-byte swizzle
@@ -748,13 +749,16 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
     p.part = nullptr;
     p.counters = nullptr;
     // M > 128: CTA pairs (each CTA dequantizes 128 of a pair's 256 columns) --
-    // unless the tiles leave SMs idle: then single-CTA tiles with K split
-    // across CTAs until about one CTA per SM (at least 8 K steps a split).
+    // unless the tiles leave SMs idle and K is long: then single-CTA tiles
+    // with K split across CTAs until about one CTA per SM (at least 8 K steps
+    // a split).  Measured: +14 to +52 % at K >= 8192, but -10 to -40 % at
+    // K = 4096, where storing and re-reading the fp32 partials costs more
+    // than the idle SMs.
     bool use_pair = M > kBM && allow_pairs;
     const int sms = sm_count();
     const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     const int pair_ctas = 2 * ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
-    if (tiles < sms && (!use_pair || pair_ctas < sms)) {
+    if (p.ksteps >= kMinSplitK / kBK && tiles < sms && (!use_pair || pair_ctas < sms)) {
         int ks = std::min(std::min(sms / tiles, p.ksteps / kMinSplitSteps), 8);
         if (ks >= 2) {
             p.ks_per = (p.ksteps + ks - 1) / ks;

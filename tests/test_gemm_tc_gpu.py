@@ -26,13 +26,14 @@ SHAPES = [
     (128, 1024, 768, 128, "int"),
     (200, 256, 520, 64, "frac"),       # N tail inside a 256-column tile, group 64
     (17, 256, 192, 128, "int"),        # smallest M the kernel takes
-    (300, 2048, 1024, None, None),     # per-column scales (one group)
+    (300, 8192, 1024, None, None),     # per-column scales (one group); K split 8 ways
     (512, 4096, 1024, 128, None),
     (1000, 1024, 4096, 128, "int"),    # ragged M
     (257, 512, 512, 64, "int"),        # second pair holds one valid row
     (129, 1024, 264, 128, None),       # smallest M on pairs; N tail of 8 columns
-    (2048, 4096, 1024, 128, None),     # 64 tiles: K split in two
-    (128, 1472, 512, 64, "frac"),      # 23 K steps split 12 + 11
+    (2048, 4096, 1024, 128, None),
+    (128, 8256, 512, 64, "frac"),      # 129 K steps split 17 x 7 + 10
+    (512, 14336, 1024, 128, "int"),    # K split 8 ways, zero points
 ]
 
 
@@ -96,7 +97,7 @@ def test_split_k_matches_unsplit(cuda_device):
     order by the tile's last CTA); it agrees with the same product computed
     unsplit, as extra rows of a larger M, far inside the gate."""
     rng = np.random.default_rng(9)
-    A, W, s, z, At, Wt, st, zt = make_case(rng, 256, 4096, 1024, 128, None, cuda_device)
+    A, W, s, z, At, Wt, st, zt = make_case(rng, 256, 8192, 1024, 128, None, cuda_device)
     C = t4_kernels.fused_w4a16_gemm_s4(At, Wt, st, None)               # 8 tiles: K split 8 ways
     big = torch.cat([At] * 20)                                          # 5120 rows: 160 tiles, no split
     Cb = t4_kernels.fused_w4a16_gemm_s4(big, Wt, st, None)

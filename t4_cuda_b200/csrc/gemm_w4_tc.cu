@@ -289,11 +289,10 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         const int quarter = warp & 3;                       // TMEM lanes this warp may read
         const int cq = (warp - 2) >> 2;                     // which 64 columns
         const int row = m0 + 32 * quarter + lane;
-        bool store = ok;
         if (p.ksplit > 1) {
             // Split K: this CTA's fp32 tile goes to its partial slot; the last
             // CTA of the tile to arrive adds the ksplit partials in split order
-            // (its own from TMEM) -- the same sum whichever CTA is last.  Every
+            // -- the same sum whichever CTA is last.  Every
             // dequant warp reaches both barriers (ok may differ per thread after
             // a timeout), and every CTA counts its arrival, so the counter is
             // back at zero when the launch ends even after an abort (whose
@@ -321,33 +320,39 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
                 __threadfence();
             }
             asm volatile("bar.sync 1, %0;" ::"n"(32 * kDqWarps) : "memory");
-            store = ok && *last_flag != 0;
-        }
-        if (store) {
+            if (ok && *last_flag != 0) {
+                // Every partial (this CTA's too) is in the workspace: sum the
+                // tile flat, consecutive threads on consecutive float4s (fully
+                // coalesced), four splits' loads in flight, in split order.
+                const int t = threadIdx.x - 64;                  // 0 .. 511
+                constexpr int kPer = kBM * kBN / 4;              // float4s in a partial
+                const float4* src = reinterpret_cast<const float4*>(p.part) + (size_t)tile * p.ksplit * kPer;
+                for (int i = t; i < kPer; i += 32 * kDqWarps) {
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int z0 = 0; z0 < p.ksplit; z0 += 4) {
+                        float4 f[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            f[u] = (z0 + u < p.ksplit) ? __ldcg(src + (size_t)(z0 + u) * kPer + i)
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            acc.x += f[u].x; acc.y += f[u].y; acc.z += f[u].z; acc.w += f[u].w;
+                        }
+                    }
+                    const int gr = m0 + (i >> 6), gc = n0 + ((i & 63) << 2);   // 64 float4s a row
+                    if (gr < p.M && gc < p.N) {       // N % 8 == 0: a float4 is all in or all out
+                        uint2 o;
+                        o.x = f2_to_h2(acc.x, acc.y);
+                        o.y = f2_to_h2(acc.z, acc.w);
+                        *reinterpret_cast<uint2*>(p.C + (size_t)gr * p.N + gc) = o;
+                    }
+                }
+            }
+        } else if (ok) {
             for (int c0 = 64 * cq; c0 < 64 * cq + 64; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
-                if (p.ksplit > 1) {
-                    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-                    const int r = 32 * quarter + lane;
-                    const float* src = p.part + ((size_t)tile * p.ksplit * kBM + r) * kBN + c0;
-                    const size_t zstride = (size_t)kBM * kBN;
-#pragma unroll
-                    for (int k = 0; k < 32; k += 4) {
-                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                        for (int z = 0; z < p.ksplit; ++z) {
-                            const float4 f = (z == (int)blockIdx.z)
-                                ? make_float4(__uint_as_float(v[k]), __uint_as_float(v[k + 1]),
-                                              __uint_as_float(v[k + 2]), __uint_as_float(v[k + 3]))
-                                : __ldcg(reinterpret_cast<const float4*>(src + z * zstride + k));
-                            acc.x += f.x; acc.y += f.y; acc.z += f.z; acc.w += f.w;
-                        }
-                        v[k] = __float_as_uint(acc.x);
-                        v[k + 1] = __float_as_uint(acc.y);
-                        v[k + 2] = __float_as_uint(acc.z);
-                        v[k + 3] = __float_as_uint(acc.w);
-                    }
-                }
                 if (row < p.M) {
                     uint16_t* crow = p.C + (size_t)row * p.N + n0 + c0;
                     if (n0 + c0 + 32 <= p.N) {

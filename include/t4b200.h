@@ -5,9 +5,10 @@
  * (passed as void*, a cudaStream_t; NULL = the legacy default stream),
  * enqueues its kernels asynchronously and returns a status code (T4B_OK = 0).
  * Nothing throws across this boundary.  The caller owns every input and output
- * buffer; the W4A16 matmul additionally uses a small scratch workspace that the
- * library allocates itself, once per (device, stream), on the first call that
- * needs it (make that first call outside CUDA-graph capture).
+ * buffer; the W4A16 matmul additionally uses a scratch workspace that the
+ * library allocates itself (cudaMalloc, never freed), once per (device,
+ * stream), on the first call that needs it -- also inside CUDA-graph capture,
+ * where it allocates at capture time -- and grows when a call needs more.
  * Element types: "f16" = IEEE binary16 (uint16 storage), "words" = uint32
  * (int32 in torch) holding packed weights.
  *

@@ -501,8 +501,13 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
         }
     }
 
-    // ---- group done: sum the row blocks of each warp column in a fixed order
+    // ---- group done: sum the row blocks of each warp column in a fixed order.
+    // A column's M partial sums sit rs = M | 1 floats apart: with an odd
+    // stride, the lanes of a warp (one column each on the read side, 8 columns
+    // x 4 batch rows on the write side) fall in distinct banks or at most two
+    // to a bank, where a stride of 16 put 16 lanes on one bank.
     const int M = p.M;
+    const int rs = M | 1;
     float* red = x.red;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -512,10 +517,10 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
             for (int e = 0; e < 4; ++e) {
                 const int col = 16 * x.bb + 4 * x.L + 2 * X + (e >> 1);
                 if (kSplitGroup) {       // batch row c, own row half only
-                    if ((e & 1) == x.bb && x.c < M) red[(x.warp * 32 + col) * M + x.c] = acc[mt][X][e];
+                    if ((e & 1) == x.bb && x.c < M) red[(x.warp * 32 + col) * rs + x.c] = acc[mt][X][e];
                 } else {
                     const int m = 8 * mt + 2 * x.c + (e & 1);
-                    if (m < M) red[(x.warp * 32 + col) * M + m] = acc[mt][X][e];
+                    if (m < M) red[(x.warp * 32 + col) * rs + m] = acc[mt][X][e];
                 }
             }
     named_barrier(1, kMathThreads);
@@ -528,9 +533,9 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
         uint32_t hv = 0;
         if (col < ncols) {
             float v = 0.f;
-            for (int k = 0; k < rbs; ++k) v += red[((w * rbs + k) * 32 + x.lane) * M + m];
+            for (int k = 0; k < rbs; ++k) v += red[((w * rbs + k) * 32 + x.lane) * rs + m];
             if (kSplitGroup)     // the second row half sits in columns 16..31 of each row block
-                for (int k = 0; k < rbs; ++k) v += red[(k * 32 + x.lane + kBoxCols) * M + m];
+                for (int k = 0; k < rbs; ++k) v += red[(k * 32 + x.lane + kBoxCols) * rs + m];
             const uint16_t h = __half_as_ushort(__float2half_rn(v));
             if (p.world == 1) p.C[(size_t)m * p.N + col_base + col] = h;
             hv = h;
@@ -901,7 +906,7 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
     p.s_split = (KW + rows_split - 1) / rows_split;
     p.act_bytes = M * (p.KWp + 2) * 16;
     p.sum_floats = (p.KWp / p.fb) * 8 * MT;
-    p.red_floats = warps * 32 * M;
+    p.red_floats = warps * 32 * (M | 1);      // row stride M | 1 (see the group epilogue)
     p.kwdiv = make_fastdiv((uint32_t)p.KWp);
     p.world = 1;
     p.rank = 0;

@@ -67,6 +67,7 @@ struct GemmParams {
 
 constexpr int kMinSplitSteps = 8;       // K steps (512 K) a split takes at least
 constexpr int kMinSplitK = 8192;        // K below which the GEMM never splits K
+constexpr int kMinPairSplitSteps = 96;  // K steps a split of a CTA pair takes at least
 
 struct GemmMaps {
     CUtensorMap a;      // A [M, K] fp16, box 64 x 128, 128-byte swizzle
@@ -519,6 +520,10 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
     const int n0 = (pair_id % n_tiles) * kCols;      // pair's columns
     const int nh = n0 + (int)rank * kHalf;           // this CTA's B columns
     const int m0 = (pair_id / n_tiles) * (2 * kRows) + (int)rank * kRows;   // this CTA's rows
+    // split K (gridDim.y splits): this pair's K steps [k_begin, k_begin + nsteps)
+    const int k_begin = blockIdx.y * p.ks_per;
+    const int nsteps = min(p.ks_per, p.ksteps - k_begin);   // >= 1: the host sizes the split so
+    volatile int* last_flag = abort_flag + 1;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTmaStages; ++s) {
@@ -547,16 +552,17 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
     if (warp == 0) {
         // ---------------- TMA producer (each CTA loads only its own operands)
         if (lane == 0) {
-            for (int i = 0; i < p.ksteps; ++i) {
+            for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kTmaStages;
                 if (i >= kTmaStages &&
                     !wait_pair(&done[s], (uint32_t)(((i / kTmaStages) & 1) ^ 1), abort_flag))
                     break;
                 uint8_t* st = base + s * kStageBytes;
-                const int srow = p.gw_steps ? i / p.gw_steps : 0;
+                const int kg = k_begin + i;                         // K step in the whole of K
+                const int srow = p.gw_steps ? kg / p.gw_steps : 0;
                 mbar_arrive_expect_tx(&full_tma[s], kABytes + kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
-                tma_load_2d(st, &maps.a, i * kBK, m0, &full_tma[s]);
-                tma_load_2d(st + kABytes, &maps.w, nh, i * (kBK / 8), &full_tma[s]);
+                tma_load_2d(st, &maps.a, kg * kBK, m0, &full_tma[s]);
+                tma_load_2d(st + kABytes, &maps.w, nh, kg * (kBK / 8), &full_tma[s]);
                 tma_load_2d(st + kABytes + kWBytes, &maps.s, nh, srow, &full_tma[s]);
                 if constexpr (HAS_ZP)
                     tma_load_2d(st + kABytes + kWBytes + kSBytes, &maps.z, nh, srow, &full_tma[s]);
@@ -568,13 +574,13 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
             // cluster addresses of done[0] in each CTA; done[s] lies 8 s bytes further
             const uint32_t done0 = map_to_rank(&done[0], 0), done1 = map_to_rank(&done[0], 1);
             bool ready = mbar_try_wait(&full_b[0], 0);
-            for (int i = 0; i < p.ksteps; ++i) {
+            for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kTmaStages, b = i % kBStages;
                 if (!ready && !wait_pair(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag)) break;
                 // peek at the next stage while this one's MMAs queue (no tcgen05 fence
                 // per stage: the barrier orders the operands, and a fence here would
                 // hold the issuer until the queued MMAs drain)
-                ready = (i + 1 < p.ksteps) &&
+                ready = (i + 1 < nsteps) &&
                         mbar_try_wait(&full_b[(i + 1) % kBStages], (uint32_t)(((i + 1) / kBStages) & 1));
                 const uint32_t a_addr = smem_addr(base + s * kStageBytes);
                 const uint32_t b_addr = smem_addr(bring + b * kBBytes);
@@ -594,7 +600,7 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
         const int n = t & (kHalf - 1);                       // column of this CTA's half
         const int j0 = (t / kHalf) * kWordsPerThread;        // first word row of the K step
         const uint32_t full_b_leader = map_to_rank(&full_b[0], 0);
-        for (int i = 0; i < p.ksteps; ++i) {
+        for (int i = 0; i < nsteps; ++i) {
             const int s = i % kTmaStages, b = i % kBStages;
             if (!wait_pair(&full_tma[s], (uint32_t)((i / kTmaStages) & 1), abort_flag)) break;
             if (i >= kBStages) {
@@ -642,7 +648,63 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
         constexpr int kColsPerWarp = kCols / (kDqWarps / 4);
         const int cq = (warp - 2) >> 2;
         const int row = m0 + 32 * quarter + lane;
-        if (ok) {
+        if (p.ksplit > 1) {
+            // Split K, as in the single-CTA kernel, per CTA: this CTA's 128 rows
+            // x 256 columns go to their partial slot; the last of the ksplit
+            // CTAs holding these rows sums the partials in split order (flat,
+            // coalesced) and writes C.  Every dequant warp reaches both
+            // barriers, and every CTA counts its arrival.
+            const int tile = 2 * pair_id + (int)rank;
+            const int r = 32 * quarter + lane;
+            float* mine = p.part + (((size_t)tile * p.ksplit + blockIdx.y) * kRows + r) * kCols;
+            if (ok) {
+                for (int c0 = kColsPerWarp * cq; c0 < kColsPerWarp * cq + kColsPerWarp; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+#pragma unroll
+                    for (int k = 0; k < 32; k += 4)
+                        __stcg(reinterpret_cast<float4*>(mine + c0 + k),
+                               make_float4(__uint_as_float(v[k]), __uint_as_float(v[k + 1]),
+                                           __uint_as_float(v[k + 2]), __uint_as_float(v[k + 3])));
+                }
+            }
+            __threadfence();
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * kDqWarps) : "memory");
+            if (threadIdx.x == 64) {
+                const bool last = atomicAdd(p.counters + tile, 1u) == (unsigned)(p.ksplit - 1);
+                if (last) p.counters[tile] = 0u;     // every CTA holding these rows has arrived
+                *last_flag = last ? 1 : 0;
+                __threadfence();
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(32 * kDqWarps) : "memory");
+            if (ok && *last_flag != 0) {
+                const int t2 = threadIdx.x - 64;                  // 0 .. 255
+                constexpr int kPer = kRows * kCols / 4;           // float4s in a partial
+                constexpr int kRow4 = kCols / 4;
+                const float4* src = reinterpret_cast<const float4*>(p.part) + (size_t)tile * p.ksplit * kPer;
+                for (int i = t2; i < kPer; i += 32 * kDqWarps) {
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int z0 = 0; z0 < p.ksplit; z0 += 4) {
+                        float4 f[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            f[u] = (z0 + u < p.ksplit) ? __ldcg(src + (size_t)(z0 + u) * kPer + i)
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            acc.x += f[u].x; acc.y += f[u].y; acc.z += f[u].z; acc.w += f[u].w;
+                        }
+                    }
+                    const int gr = m0 + i / kRow4, gc = n0 + (i % kRow4) * 4;
+                    if (gr < p.M && gc < p.N) {       // N % 8 == 0: a float4 is all in or all out
+                        uint2 o;
+                        o.x = f2_to_h2(acc.x, acc.y);
+                        o.y = f2_to_h2(acc.z, acc.w);
+                        *reinterpret_cast<uint2*>(p.C + (size_t)gr * p.N + gc) = o;
+                    }
+                }
+            }
+        } else if (ok) {
             for (int c0 = kColsPerWarp * cq; c0 < kColsPerWarp * cq + kColsPerWarp; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
@@ -695,7 +757,7 @@ int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
     }
     cudaLaunchConfig_t cfg = {};
     const int pairs = ((p.N + kCols - 1) / kCols) * ((p.M + 2 * kRows - 1) / (2 * kRows));
-    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.gridDim = dim3(2 * pairs, p.ksplit, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -753,27 +815,38 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
     p.ks_per = p.ksteps;
     p.part = nullptr;
     p.counters = nullptr;
-    // M > 128: CTA pairs (each CTA dequantizes 128 of a pair's 256 columns) --
-    // unless the tiles leave SMs idle and K is long: then single-CTA tiles
-    // with K split across CTAs until about one CTA per SM (at least 8 K steps
-    // a split).  Measured: +14 to +52 % at K >= 8192, but -10 to -40 % at
-    // K = 4096, where storing and re-reading the fp32 partials costs more
-    // than the idle SMs.
+    // M > 128: CTA pairs (each CTA dequantizes 128 of a pair's 256 columns).
+    // When the tiles (or pairs) leave SMs idle and K is long, K is split
+    // across CTAs (or pairs) until about one CTA per SM (at least 8 K steps a
+    // split).  Measured: gains at K >= 8192, but losses at K = 4096, where
+    // storing and re-reading the fp32 partials costs more than the idle SMs.
     bool use_pair = M > kBM && allow_pairs;
     const int sms = sm_count();
     const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     const int pair_ctas = 2 * ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
     if (p.ksteps >= kMinSplitK / kBK && tiles < sms && (!use_pair || pair_ctas < sms)) {
-        int ks = std::min(std::min(sms / tiles, p.ksteps / kMinSplitSteps), 8);
+        auto split_of = [&](int ctas) { return std::min(std::min(sms / ctas, p.ksteps / kMinSplitSteps), 8); };
+        // M > 128 splits the CTA pairs (half a single CTA's dequant per SM)
+        // when each split keeps a long K run; with short runs the pair's
+        // larger fixed cost wins out (measured against single CTAs: +5-10 % at
+        // 224 K steps a split, +1-3 % at 112, -2-10 % at 64, -16 % at 16), and
+        // single CTAs split instead.  Either way a partial
+        // is one CTA's 128 x 256 accumulator.
+        if (use_pair) {
+            const int kp = split_of(pair_ctas);
+            const bool pair_split = kp >= 2 && (p.ksteps + kp - 1) / kp >= kMinPairSplitSteps;
+            if (!pair_split && split_of(tiles) >= 2) use_pair = false;
+        }
+        const int ctas = use_pair ? pair_ctas : tiles;
+        const int ks = split_of(ctas);
         if (ks >= 2) {
             p.ks_per = (p.ksteps + ks - 1) / ks;
             p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;      // no empty split
             Workspace ws;
-            const int st = acquire_workspace(stream, (size_t)tiles, (size_t)tiles * p.ksplit * kBM * kBN, &ws);
+            const int st = acquire_workspace(stream, (size_t)ctas, (size_t)ctas * p.ksplit * kBM * kBN, &ws);
             if (st != T4B_OK) return st;
             p.part = ws.part;
             p.counters = ws.counters;
-            use_pair = false;
         }
     }
     const uint32_t wbox = use_pair ? pair::kHalf : kBN;

@@ -34,6 +34,7 @@ SHAPES = [
     (2048, 4096, 1024, 128, None),
     (128, 8256, 512, 64, "frac"),      # 129 K steps split 17 x 7 + 10
     (512, 14336, 1024, 128, "int"),    # K split 8 ways, zero points
+    (512, 14336, 4096, 128, "int"),    # CTA pairs split K in two (112 K steps each), zero points
 ]
 
 

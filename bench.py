@@ -42,6 +42,7 @@ sys.path.insert(0, ROOT)
 import torch  # noqa: E402
 
 METRIC = "W4A16 GEMV HBM GB/s (% of 8 TB/s) at M=1; GEMM TFLOPS at M=4096"
+WORKLOAD = "decode: Llama-3-8B token, 32 layers x 7 projections, M=1, s4 g128"
 GROUP = 128
 N_LAYERS = 32
 PROJ = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
@@ -668,7 +669,7 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16 (int4 weights, fp32 accumulate)",
         "data": "synthetic",
-        "config": {"workload": "decode: Llama-3-8B token, 32 layers x 7 projections, M=1, s4 g128",
+        "config": {"workload": WORKLOAD,
                    "M": M, "group": GROUP, "layers_per_step": N_LAYERS, "distinct_weight_layers": pool,
                    "weight_pool_bytes": pool * layer_bytes_local, "l2_bytes": l2,
                    "l2_policy": "weights rotate through a pool >= 4x L2 (inputs larger than L2)",
@@ -767,8 +768,9 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / args.steps, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (fp16 weights)",
             "data": "synthetic",
-            "config": {"workload": "decode: Llama-3-8B projections, M=1, s4 g128 (one projection per step)",
-                       "M": M, "group": GROUP},
+            "config": {"workload": WORKLOAD, "M": M, "group": GROUP, "layers_per_step": N_LAYERS,
+                       "reference_step": "a bounded sample: one projection per step, rotating q,k,v,o,gate,up,down "
+                                         "(GB/s of algorithmic bytes, the same unit as the full step)"},
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
                              "kind": "port",
                              "sample": "one Llama-3-8B projection per step, rotating q,k,v,o,gate,up,down"},

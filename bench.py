@@ -19,9 +19,9 @@ uses NCCL all-gather instead): the same token, so "scaling" is "strong".
 
 The line also carries "decode_batch" (one GPU): the four projection shapes
 at M in {1, 4, 8, 16}, one launch at a time; "gemm_sweep" (one GPU): the
-same shapes at M in {512, 2048, 4096} on the tcgen05 GEMM; and "sharded_70b": Llama-3-70B layer projections
-column-sharded over the same N GPUs at M in {1, 16, 256, 4096} (see
-sharded_70b).
+same shapes at M in {512, 2048, 4096} on the tcgen05 GEMM; and
+"sharded_70b": Llama-3-70B layer projections column-sharded over the same
+N GPUs at M in {1, 16, 256, 4096} (see sharded_70b).
 
 --impl reference times the reference's CPU dequant + matmul path
 (tests/test_fused_gemm_correctness.py:22-36, restated in oracle/cpu_path.py)

@@ -1,7 +1,7 @@
 // TMA, mbarrier and programmatic-dependent-launch helpers for sm_100a.
 //
-// No TMA load here uses .multicast::cluster: every copy reads this GPU's own
-// memory into this CTA's shared memory.
+// No TMA load here is a cluster multicast: every copy reads this GPU's own
+// memory into this CTA's shared memory only.
 #pragma once
 
 #include <cuda.h>

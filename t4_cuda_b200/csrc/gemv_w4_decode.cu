@@ -22,10 +22,13 @@
 //   group scales (and one of zero points) over the stage's rows and the
 //   group's 64 or 32 columns -- a handful of large copies per stage, because the
 //   thread that issues a copy stalls while the SM's copy engine is busy.
-//   All of it is constant data, so the first stages are issued at kernel
-//   entry, before griddepcontrol.wait, and stream in while the previous
-//   kernel in the stream drains (two CTAs fit on an SM: one computing, one
-//   prefetching).  A dedicated producer warp refills the slots: a copy
+//   All of it is constant data, so every stage the ring holds is issued at
+//   kernel entry, before griddepcontrol.wait, and streams in while the
+//   previous kernel in the stream drains.  One CTA fills an SM: a ring as
+//   deep as shared memory allows keeps ~200 KB per SM in flight, which the
+//   copy engine needs to stream 64-byte box rows at full rate (measured in
+//   the decode step: 1.62 ms against 2.24 ms with two co-resident CTAs of
+//   half the depth).  A dedicated producer warp refills the slots: a copy
 //   issue can stall for hundreds of cycles while the copy engine is busy, and
 //   a math warp doing it would put that stall on every stage's critical path.
 //   The math warps release a slot by arriving on its "empty" barrier.
@@ -48,6 +51,7 @@
 //   with the activation sum:
 //       y += scale * (sum (o + q) a  -  (o + z) sum a),   o = 64 or 72.
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "tma.cuh"
@@ -156,17 +160,34 @@ __device__ __forceinline__ uint2 lds64(uint32_t addr) {
     return v;
 }
 
+// 32-bit integer multiplies: the low word for a left shift and the high word
+// for a right shift by a constant.  They issue to the FMA pipe, while shifts
+// and LOP3 share the integer pipe, which the unpacking below otherwise
+// saturates (measured: +16 % per-SM unpack throughput over plain shifts).
+__device__ __forceinline__ uint32_t mul_lo_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.lo.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t mul_hi_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 // Nibble pairs (0,4), (1,5), (2,6), (3,7) of w as fp16x2 offset integers:
-// 64 + u (unsigned) or 72 + s (signed two's complement nibble).
+// 64 + u (unsigned) or 72 + s (signed two's complement nibble).  Each pair
+// is moved to bits 4-7 / 20-23 (w * 16, w, w / 16, w / 256) and merged into
+// the mantissa of 64.0 by one LOP3.
 template <bool SIGNED>
 __device__ __forceinline__ void unpack_offset64(uint32_t w, uint32_t (&e)[4]) {
     constexpr uint32_t kMask = 0x00F000F0u;
     constexpr uint32_t kMagic = SIGNED ? 0x54805480u : 0x54005400u;
     constexpr int kLut = SIGNED ? 0x6A : 0xEA;     // (a & b) ^ c  /  (a & b) | c
-    e[0] = lop3<kLut>(w << 4, kMask, kMagic);
+    e[0] = lop3<kLut>(mul_lo_u32(w, 16u), kMask, kMagic);
     e[1] = lop3<kLut>(w, kMask, kMagic);
-    e[2] = lop3<kLut>(w >> 4, kMask, kMagic);
-    e[3] = lop3<kLut>(w >> 8, kMask, kMagic);
+    e[2] = lop3<kLut>(mul_hi_u32(w, 1u << 28), kMask, kMagic);
+    e[3] = lop3<kLut>(mul_hi_u32(w, 1u << 24), kMask, kMagic);
 }
 
 // Word-row offset (0..15) of lane column c in row step j of a warp's 16 rows;
@@ -607,13 +628,10 @@ __device__ __forceinline__ void gather_complete(const DecodeParams& p) {
     }
 }
 
-// MINB: CTAs per SM the register budget is sized for.  2 leaves room for the
-// next kernel's CTA to start early (programmatic dependent launch) on every
-// SM; 1 gives each thread twice the registers, which schedules the math
-// better, and is used when the grid covers at most half the SMs -- the next
-// kernel then starts early on the others.
-template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int MINB>
-__global__ void __launch_bounds__(Shape<MT>::kThreads, MINB)
+// One CTA per SM (its ring takes the SM's shared memory), so the register
+// budget is that of one CTA.
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8>
+__global__ void __launch_bounds__(Shape<MT>::kThreads, 1)
 gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p) {
     using S = Shape<MT>;
     constexpr int kWarps = S::kWarps;
@@ -784,10 +802,10 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     if (p.world > 1 && p.barrier) gather_complete(p);
 }
 
-template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int MINB>
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8>
 int launch(const DecodeMaps& maps, const DecodeParams& p, size_t smem,
            cudaStream_t stream) {
-    auto kern = gemv_w4_decode_kernel<MT, SIGNED, HAS_ZP, FB8, MINB>;
+    auto kern = gemv_w4_decode_kernel<MT, SIGNED, HAS_ZP, FB8>;
     static int configured = 0;   // largest dynamic shared memory set so far for this instantiation
     if ((int)smem > configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -809,42 +827,35 @@ int launch(const DecodeMaps& maps, const DecodeParams& p, size_t smem,
     return T4B_OK;
 }
 
-template <int MT, bool SIGNED, int MINB>
+template <int MT, bool SIGNED>
 int dispatch_zp(bool zp, bool fb8, const DecodeMaps& maps, const DecodeParams& p, size_t smem,
                 cudaStream_t stream) {
-    if (zp) return fb8 ? launch<MT, SIGNED, true, true, MINB>(maps, p, smem, stream)
-                       : launch<MT, SIGNED, true, false, MINB>(maps, p, smem, stream);
-    return fb8 ? launch<MT, SIGNED, false, true, MINB>(maps, p, smem, stream)
-               : launch<MT, SIGNED, false, false, MINB>(maps, p, smem, stream);
+    if (zp) return fb8 ? launch<MT, SIGNED, true, true>(maps, p, smem, stream)
+                       : launch<MT, SIGNED, true, false>(maps, p, smem, stream);
+    return fb8 ? launch<MT, SIGNED, false, true>(maps, p, smem, stream)
+               : launch<MT, SIGNED, false, false>(maps, p, smem, stream);
 }
 
-int dispatch(bool is_signed, bool zp, bool fb8, int MT, bool few_ctas, const DecodeMaps& maps, const DecodeParams& p,
-             size_t smem, cudaStream_t stream) {
-    if (MT == 1) {
-        if (few_ctas)
-            return is_signed ? dispatch_zp<1, true, 1>(zp, fb8, maps, p, smem, stream)
-                             : dispatch_zp<1, false, 1>(zp, fb8, maps, p, smem, stream);
-        return is_signed ? dispatch_zp<1, true, 2>(zp, fb8, maps, p, smem, stream)
-                         : dispatch_zp<1, false, 2>(zp, fb8, maps, p, smem, stream);
-    }
-    return is_signed ? dispatch_zp<2, true, 2>(zp, fb8, maps, p, smem, stream)
-                     : dispatch_zp<2, false, 2>(zp, fb8, maps, p, smem, stream);
+int dispatch(bool is_signed, bool zp, bool fb8, int MT, const DecodeMaps& maps, const DecodeParams& p, size_t smem,
+             cudaStream_t stream) {
+    if (MT == 1)
+        return is_signed ? dispatch_zp<1, true>(zp, fb8, maps, p, smem, stream)
+                         : dispatch_zp<1, false>(zp, fb8, maps, p, smem, stream);
+    return is_signed ? dispatch_zp<2, true>(zp, fb8, maps, p, smem, stream)
+                     : dispatch_zp<2, false>(zp, fb8, maps, p, smem, stream);
 }
 
-// Shared memory an SM offers two co-resident CTAs, and one CTA alone.
-void smem_budget(size_t* two, size_t* one) {
-    static size_t b2 = 0, b1 = 0;
-    if (!b1) {
-        int dev = 0, per_sm = 0, optin = 0, reserved = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
-        b2 = (size_t)(per_sm / 2 - reserved);
-        b1 = (size_t)optin;
-    }
-    *two = b2;
-    *one = b1;
+// Dynamic shared memory one CTA may use on the current device (cached per device).
+size_t smem_budget() {
+    static std::atomic<int> cached[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[dev].load(std::memory_order_relaxed) > 0)
+        return (size_t)cached[dev].load(std::memory_order_relaxed);
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (dev >= 0 && dev < 64) cached[dev].store(optin, std::memory_order_relaxed);
+    return (size_t)optin;
 }
 
 }  // namespace
@@ -929,26 +940,18 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
     const int weight_bytes = warps * 2048;
     p.slot_bytes = (weight_bytes + p.s_bytes * (Z ? 2 : 1) + 1023) / 1024 * 1024;
     const size_t fixed = 1024 + (size_t)p.act_bytes + 4 * (size_t)(p.sum_floats + p.red_floats) + kMaxStages * 16 + 8 + 16;
-    // two CTAs per SM (one computing, one prefetching the next kernel's
-    // stages) when the ring still gets 2+ stages; else one CTA, deeper ring
-    size_t two = 0, one = 0;
-    smem_budget(&two, &one);
-    int stages = fixed < two ? (int)((two - fixed) / p.slot_bytes) : 0;
-    if (stages > 8) stages = 8;
-    if (stages < 2) {
-        stages = fixed < one ? (int)((one - fixed) / p.slot_bytes) : 0;
-        if (stages > kMaxStages) stages = kMaxStages;
-    }
+    // one CTA per SM with the deepest ring shared memory allows
+    const size_t budget = smem_budget();
+    int stages = fixed < budget ? (int)((budget - fixed) / p.slot_bytes) : 0;
+    if (stages > kMaxStages) stages = kMaxStages;
     if (stages < 2) return T4B_ERR_UNSUPPORTED;
     if (plan_only) return T4B_OK;
     p.stages = stages;
-    // A CTA whose weights fit in the ring fetches all of them before the
-    // previous kernel ends.  One that must stream more than a ring's worth
-    // fetches a single stage early: a deep early prefetch from every SM would
-    // queue ahead of the previous kernel's own loads (its refills and its
-    // activations) and delay the very kernel it waits for.
-    const long long cta_bytes = (long long)((p.T + p.G - 1) / p.G) * kBoxCols * KW * 4;
-    p.early = (cta_bytes <= (long long)stages * weight_bytes) ? stages : (stages > 2 ? 2 : 1);
+    // Every stage the ring holds is fetched before the previous kernel ends:
+    // with one CTA per SM nothing of the next kernel competes for the copy
+    // engine, and the deeper the early fetch the less of the stream is left
+    // once the activations are in.
+    p.early = stages;
     const size_t smem = fixed + (size_t)stages * p.slot_bytes;
 
     DecodeMaps maps;
@@ -968,7 +971,7 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
         maps.z_narrow = maps.s_narrow;
         maps.z_split = maps.s_split;
     }
-    return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, 2 * p.G <= sm_count(), maps, p, smem, stream);
+    return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, maps, p, smem, stream);
 }
 
 int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,

@@ -54,12 +54,20 @@ int t4b_last_cuda_error(void);
 int t4b_version(void);
 
 /* Reads (and, if `clear`, resets) the library's device error words on the
- * current device -- the decode GEMV's (one per device) ORed with the one in the
- * workspace kept for `stream` (if any): bit 0 = a kernel gave up a bounded wait
- * (its output is then invalid).  Synchronizes `stream`; do not call while the
- * stream is being captured.  No counterpart in the reference, which has no
- * device-side error reporting. */
+ * current device -- the decode GEMV's and the prefill GEMM's (one each per
+ * device), the allocation-free GEMV's (in its fixed scratch array) and the one
+ * in the workspace kept for `stream` (if any), ORed: bit 0 = a kernel gave up
+ * a bounded wait (its output is then invalid).  Synchronizes `stream`; do not
+ * call while the stream is being captured.  No counterpart in the reference,
+ * which has no device-side error reporting. */
 int t4b_device_error(void* stream, unsigned* out, int clear);
+
+/* Bytes of the workspace this library holds for `stream` on the current
+ * device (0 if it has made none): the split-tile GEMV and the split-K GEMM
+ * cudaMalloc one on their first call on a stream.  A diagnostic with no
+ * counterpart in the reference, for callers that must know whether the library
+ * allocated device memory. */
+int t4b_workspace_bytes(void* stream, size_t* bytes);
 
 /* Kernel selection for the W4A16 matmul (argument of t4b_set_gemv_kernel). */
 enum {
@@ -137,7 +145,8 @@ int t4b_fused_w4a16_gemm_s4(const void* A, const void* W_packed, const void* sca
  * device current); make that first call before any stream capture.  Every call
  * shares the one array: calls that overlap on the GPU (different streams,
  * concurrent graph replays) race and give wrong results.  Each call clears the
- * array's flags and error word on `stream` before its kernel. */
+ * array's flags on `stream` before its kernel; its error word (bit 0: a bounded
+ * wait gave up and C is invalid) stays set until t4b_device_error clears it. */
 int t4b_fused_w4a16_gemv_noalloc(const void* A, const void* W_packed, const void* scales,
                                  const void* zero_points, void* C, int M, int N, int K,
                                  int group_size, int is_signed, void* stream);

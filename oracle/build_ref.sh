@@ -3,14 +3,23 @@
 # where they lie in the reference checkout, into oracle/_ref/libt4ref.so -- a
 # GPU-side checker for the tests (never shipped, never measured).
 #
-# usage: oracle/build_ref.sh [reference checkout, default /root/reference]
+# usage: oracle/build_ref.sh [--if-present] [reference checkout]
+#   The checkout is the argument, else $T4B_REFERENCE, else /root/reference
+#   (where this build container mounts it).  With --if-present a missing
+#   checkout is not an error: nothing is built.
 #
 # Compiles src/kernels/{lop3_dequant,fused_w4a16_gemm,h17_mega_kernel}.cu of the
 # reference plus oracle/ref_shim.cu (C-ABI forwarding of the launchers) for
 # sm_100a.  Nothing is copied out of the reference tree; the output goes to
 # oracle/_ref/ only (git-ignored; it travels with the working tree).
 set -euo pipefail
-REF=${1:-/root/reference}
+IF_PRESENT=0
+if [ "${1:-}" = "--if-present" ]; then IF_PRESENT=1; shift; fi
+REF=${1:-${T4B_REFERENCE:-/root/reference}}
+if [ ! -d "$REF/src/kernels" ]; then
+    if [ "$IF_PRESENT" = 1 ]; then echo "build_ref: no reference checkout at $REF; skipped"; exit 0; fi
+    echo "build_ref: no reference checkout at $REF" >&2; exit 1
+fi
 HERE=$(cd "$(dirname "$0")" && pwd)
 OUT="$HERE/_ref"
 NVCC=${NVCC:-$(command -v nvcc || echo /usr/local/cuda/bin/nvcc)}

@@ -82,6 +82,8 @@ def load():
         lib.t4b_set_gemv_kernel.restype = ctypes.c_int
         lib.t4b_device_error.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
         lib.t4b_device_error.restype = ctypes.c_int
+        lib.t4b_workspace_bytes.argtypes = [_vp, ctypes.POINTER(ctypes.c_size_t)]
+        lib.t4b_workspace_bytes.restype = ctypes.c_int
         _lib = lib
     return _lib
 

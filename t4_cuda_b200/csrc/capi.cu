@@ -51,6 +51,20 @@ int sm_count() {
     return n;
 }
 
+int ensure_dynamic_smem(const void* kernel, int bytes, SmemLimit* limit) {
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    if (dev < 0 || dev >= 64) return T4B_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(mu);
+    if (limit->bytes[dev] >= bytes) return T4B_OK;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    limit->bytes[dev] = bytes;
+    return T4B_OK;
+}
+
 int acquire_workspace(cudaStream_t stream, size_t counter_words, size_t part_floats, Workspace* ws) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -218,6 +232,35 @@ bool make_tmap_2d_ex(CUtensorMap* map, bool fp16, const void* base, uint64_t row
     return true;
 }
 
+bool make_tmap_tiles_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t tile_cols,
+                        uint32_t box_tiles, uint32_t box_rows) {
+    // cached with the 2-D maps; fp16 = 2 marks this kind of map
+    const TmapKey key{base, rows, cols, box_rows, box_tiles * 1024u + tile_cols, 128, 256, 2};
+    TmapEntry& slot = t_tmap_cache[tmap_hash(key)];
+    if (slot.valid && slot.key == key) {
+        *map = slot.map;
+        return true;
+    }
+    slot.valid = false;
+    auto fn = encode_fn();
+    if (!fn) return false;
+    // the view holds the whole tiles of a row (a trailing partial tile is left out)
+    if (tile_cols == 0 || cols < tile_cols || tile_cols * 4 != 128) return false;
+    if ((cols * 4) % 16 != 0 || (reinterpret_cast<uintptr_t>(base) % 16) != 0) return false;
+    cuuint64_t dims[3] = {tile_cols, cols / tile_cols, rows};   // floor: whole tiles only
+    cuuint64_t strides[2] = {(cuuint64_t)tile_cols * 4, cols * 4};
+    cuuint32_t box[3] = {tile_cols, box_tiles, box_rows};
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    slot.key = key;
+    slot.map = *map;
+    slot.valid = true;
+    return true;
+}
+
 }  // namespace t4b
 
 extern "C" {
@@ -290,6 +333,11 @@ int t4b_device_error(void* stream, unsigned* out, int clear) {
     st = t4b::gemm_tc_device_error(s, &gemm, clear != 0);
     if (st != T4B_OK) return st;
     *out |= gemm;
+    // and the allocation-free GEMV, in its fixed scratch array
+    unsigned fixed = 0;
+    st = t4b::static_scratch_error(s, &fixed, clear != 0);
+    if (st != T4B_OK) return st;
+    *out |= fixed;
     // the split-tile GEMV keeps one in the workspace of each stream
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -307,6 +355,19 @@ int t4b_device_error(void* stream, unsigned* out, int clear) {
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return t4b::record_cuda_error(e);
     *out |= word;
+    return T4B_OK;
+}
+
+int t4b_workspace_bytes(void* stream, size_t* bytes) {
+    if (!bytes) return T4B_ERR_NULL_POINTER;
+    *bytes = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return t4b::record_cuda_error(e);
+    std::lock_guard<std::mutex> lock(t4b::g_ws_mutex);
+    auto it = t4b::g_ws.find({dev, static_cast<cudaStream_t>(stream)});
+    if (it != t4b::g_ws.end() && it->second.base)
+        *bytes = t4b::kHeaderBytes + (it->second.counter_words + it->second.part_floats) * 4;
     return T4B_OK;
 }
 

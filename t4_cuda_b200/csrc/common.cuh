@@ -25,6 +25,17 @@ inline int check_launch() {
 // Streaming-multiprocessor count of the current device (cached per device).
 int sm_count();
 
+// Per-device record of the dynamic shared memory a kernel has been allowed
+// (cudaFuncAttributeMaxDynamicSharedMemorySize applies to the device that is
+// current when it is set, so each device needs its own call).
+struct SmemLimit {
+    int bytes[64] = {0};
+};
+// Raises `kernel`'s dynamic shared-memory limit on the current device to at
+// least `bytes` (a no-op once it is there); thread-safe.  T4B_OK or the
+// recorded CUDA error.
+int ensure_dynamic_smem(const void* kernel, int bytes, SmemLimit* limit);
+
 // TMA-streamed, SM-balanced W4A16 GEMV (gemv_w4_stream.cu).  Returns
 // T4B_ERR_UNSUPPORTED when the shape / alignment does not suit it.
 int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
@@ -46,6 +57,8 @@ int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const vo
 // Reads (and optionally clears) the decode GEMV's device error word on the
 // current device; synchronizes `stream`.
 int decode_device_error(cudaStream_t stream, unsigned* out, bool clear);
+// Same for the allocation-free GEMV's word (in its fixed scratch array).
+int static_scratch_error(cudaStream_t stream, unsigned* out, bool clear);
 
 // Prefill GEMM on tcgen05 / TMEM (M > 16, K % 64 == 0, group % 64 == 0);
 // T4B_ERR_UNSUPPORTED (without launching) for shapes it does not take.

@@ -749,12 +749,9 @@ template <bool SIGNED, bool HAS_ZP>
 int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
     auto kern = gemm_w4_tc_pair_kernel<SIGNED, HAS_ZP>;
     const size_t smem = 1024 + (size_t)kRingBytes + kBarriers * 8 + 16;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        configured = true;
-    }
+    static SmemLimit limit;     // per instantiation, per device
+    const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
+    if (st != T4B_OK) return st;
     cudaLaunchConfig_t cfg = {};
     const int pairs = ((p.N + kCols - 1) / kCols) * ((p.M + 2 * kRows - 1) / (2 * kRows));
     cfg.gridDim = dim3(2 * pairs, p.ksplit, 1);
@@ -779,12 +776,9 @@ template <bool SIGNED, bool HAS_ZP>
 int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
     auto kern = gemm_w4_tc_kernel<SIGNED, HAS_ZP>;
     const size_t smem = 1024 + (size_t)kRingBytes + kBarriers * 8 + 16;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        configured = true;
-    }
+    static SmemLimit limit;     // per instantiation, per device
+    const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
+    if (st != T4B_OK) return st;
     dim3 grid((p.N + kBN - 1) / kBN, (p.M + kBM - 1) / kBM, p.ksplit);
     kern<<<grid, kThreads, smem, stream>>>(maps, p);
     return check_launch();

@@ -466,12 +466,9 @@ int launch(const CUtensorMap& tmap, const StreamParams& p, int ychunks, bool pdl
     const size_t smem = 1024 + kStages * kStageBytes + (size_t)kWarps * kTileN * (MR + 1) * 4 + kStages * 8 +
                         kStages * 4 + 16;
     auto kern = gemv_w4_stream_kernel<MT, SIGNED, HAS_ZP>;
-    static bool configured = false;   // per instantiation; setting the attribute twice is harmless
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        configured = true;
-    }
+    static SmemLimit limit;     // per instantiation, per device
+    const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
+    if (st != T4B_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.G, ychunks, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -572,10 +569,12 @@ int gemv_w4_stream(bool is_signed, const void* A, const void* W, const void* S, 
 //
 // Layout of the array: bytes [0, 256) hold the device error word, then the
 // per-segment "published" flags, then (at a 256-byte boundary) the partial
-// sums of split tiles.  Each call clears the error word and the flags with
-// one cudaMemsetAsync; the partials need no clearing (every one is written
-// before it is read).  All calls share the array, so two calls that overlap
-// on the GPU (different streams, or concurrent graph replays) race.
+// sums of split tiles.  Each call clears the flags it uses with one
+// cudaMemsetAsync; the error word stays set once a bounded wait has given up
+// (t4b_device_error reads and clears it), and the partials need no clearing
+// (every one is written before it is read).  All calls share the array, so
+// two calls that overlap on the GPU (different streams, or concurrent graph
+// replays) race.
 constexpr size_t kStaticScratchBytes = size_t(4) << 20;   // 4 MiB
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
@@ -598,6 +597,18 @@ int static_scratch_address(unsigned char** out) {
     }
     *out = addr[dev];
     return T4B_OK;
+}
+
+// Reads (and optionally clears) the allocation-free GEMV's error word on the
+// current device; synchronizes `stream`.
+int static_scratch_error(cudaStream_t stream, unsigned* out, bool clear) {
+    unsigned char* base = nullptr;
+    int st = static_scratch_address(&base);
+    if (st != T4B_OK) return st;
+    cudaError_t e = cudaMemcpyAsync(out, base, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(base, 0, sizeof(unsigned), stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e == cudaSuccess ? T4B_OK : record_cuda_error(e);
 }
 
 }  // namespace t4b
@@ -625,7 +636,7 @@ extern "C" int t4b_fused_w4a16_gemv_noalloc(const void* A, const void* W_packed,
     unsigned char* base = nullptr;
     st = static_scratch_address(&base);
     if (st != T4B_OK) return st;
-    cudaError_t e = cudaMemsetAsync(base, 0, head, stream);
+    cudaError_t e = cudaMemsetAsync(base + 256, 0, head - 256, stream);   // the flags, not the error word
     if (e != cudaSuccess) return record_cuda_error(e);
     p.err = reinterpret_cast<unsigned*>(base);
     p.flags = reinterpret_cast<unsigned*>(base + 256);

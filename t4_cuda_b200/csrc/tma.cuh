@@ -28,6 +28,19 @@ bool make_tmap_f16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 bool make_tmap_2d_ex(CUtensorMap* map, bool fp16, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
                      uint32_t box_cols, int swizzle_bytes, int l2_promotion_bytes);
 
+// 3-D view of a row-major matrix of 4-byte elements (rows x cols) as
+// (tile_cols, floor(cols / tile_cols), rows) -- whole tiles only -- with a box
+// of tile_cols x box_tiles x box_rows and 128-byte swizzle.  tile_cols * 4
+// must be exactly 128: the swizzle lays every box row out at a 128-byte
+// pitch, so a narrower inner dimension would take more shared memory than
+// the box's bytes.  One box row is box_tiles * tile_cols consecutive elements
+// of a matrix row, so a box of adjacent tiles is fetched as wide contiguous
+// rows; it lands in shared memory as [box_rows][box_tiles * 128 B] with the
+// 16-byte units of each 128-byte line permuted by the line's index (mod 8).
+// Returns false if encoding fails.
+bool make_tmap_tiles_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t tile_cols,
+                        uint32_t box_tiles, uint32_t box_rows);
+
 // --------------------------------------------------------------- device side
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -95,6 +108,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             smem_addr(dst)),
         "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// 3-D TMA load of one box (coordinates innermost first).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
 }
 

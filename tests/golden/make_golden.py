@@ -2,9 +2,10 @@
 """Generate the golden vectors under tests/golden/ from the reference's OWN
 CPU functions (kridaydave/t4-cuda), imported from a read-only checkout.
 
-Run in a container that has the reference checkout:
+Run in a container that has the reference checkout, passing its location
+(or setting T4B_REFERENCE):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference checkout>
 
 The outputs are committed; the tests read only the outputs, never the
 reference.  Every case records which reference function produced it.
@@ -266,7 +267,9 @@ def int3_cases(th17):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("T4B_REFERENCE")
+    if not ref_root:
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set T4B_REFERENCE)")
     tdc, tfg, th17, vd, vfg = _import_reference(ref_root)
 
     cases = dequant_cases(tdc, vd)

@@ -490,6 +490,70 @@ __device__ __forceinline__ void stage_math(const DecodeParams& p, const LaneOffs
     }
 }
 
+// The math of two ring stages for this warp, interleaved row step by row
+// step: the two stages' loads, unpacking and MMAs are independent chains, so
+// one warp has twice the work in flight between two barrier waits.
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int KIND>
+__device__ __forceinline__ void stage_math2(const DecodeParams& p, const LaneOffsets<MT>& lo, float (&acc)[MT][2][4],
+                                            uint32_t st0, uint32_t st1, int row0, int row1, uint32_t sum_base) {
+    constexpr bool kSplitGroup = KIND == kSplit;
+    const uint32_t zdelta = (uint32_t)p.s_bytes;
+    const uint32_t st[2] = {st0, st1};
+    const int r0[2] = {row0, row1};
+    float dg[2][MT][2][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint4 wv[2], av[2][MT];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            wv[h] = lds128(st[h] + lo.woff[j]);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) av[h][mt] = lds128(lo.aoff[mt][j] + (uint32_t)r0[h] * 16);
+        }
+        const bool first = (j == 0) || (j == 2 && FB8);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t e0[4], e1[4], e2[4], e3[4];
+            unpack_offset64<SIGNED>(wv[h].x, e0);
+            unpack_offset64<SIGNED>(wv[h].y, e1);
+            unpack_offset64<SIGNED>(wv[h].z, e2);
+            unpack_offset64<SIGNED>(wv[h].w, e3);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                if (first) {
+                    mma_16816_zero(dg[h][mt][0], e0[0], e1[0], e0[1], e1[1], av[h][mt].x, av[h][mt].y);
+                    mma_16816_zero(dg[h][mt][1], e2[0], e3[0], e2[1], e3[1], av[h][mt].x, av[h][mt].y);
+                } else {
+                    mma_16816(dg[h][mt][0], e0[0], e1[0], e0[1], e1[1], av[h][mt].x, av[h][mt].y);
+                    mma_16816(dg[h][mt][1], e2[0], e3[0], e2[1], e3[1], av[h][mt].x, av[h][mt].y);
+                }
+                mma_16816(dg[h][mt][0], e0[2], e1[2], e0[3], e1[3], av[h][mt].z, av[h][mt].w);
+                mma_16816(dg[h][mt][1], e2[2], e3[2], e2[3], e3[3], av[h][mt].z, av[h][mt].w);
+            }
+        }
+        if (j == 1 && FB8) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t b8 = (uint32_t)((r0[h] + lo.lane_row) >> 3);
+                flush<MT, SIGNED, HAS_ZP, kSplitGroup>(acc, dg[h], st[h] + lo.soff[0], st[h] + lo.soff[0] + zdelta,
+                                                       sum_base + b8 * (32 * MT));
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (FB8) {
+            const uint32_t b8 = (uint32_t)((r0[h] + lo.lane_row) >> 3) + 1;
+            flush<MT, SIGNED, HAS_ZP, kSplitGroup>(acc, dg[h], st[h] + lo.soff[1], st[h] + lo.soff[1] + zdelta,
+                                                   sum_base + b8 * (32 * MT));
+        } else {
+            const uint32_t b16 = (uint32_t)((r0[h] + lo.lane_row) >> 4);
+            flush<MT, SIGNED, HAS_ZP, kSplitGroup>(acc, dg[h], st[h] + lo.soff[0], st[h] + lo.soff[0] + zdelta,
+                                                   sum_base + b16 * (32 * MT));
+        }
+    }
+}
+
 // Bounded wait for the stage in the current slot; an abort (timeout) is
 // recorded once and every later stage is skipped.
 __device__ __forceinline__ void wait_stage(MathCtx& x, uint32_t slot, uint32_t phase) {
@@ -542,12 +606,10 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
         next_slot(p, slot1, phase1);
         wait_stage(x, slot, phase);
         wait_stage(x, slot1, phase1);
-        if (!x.aborted) {
-            stage_math<MT, SIGNED, HAS_ZP, FB8, KIND>(p, lo, acc, x.ring_a + slot * (uint32_t)p.slot_bytes, ks * rows,
-                                                     sum_base);
-            stage_math<MT, SIGNED, HAS_ZP, FB8, KIND>(p, lo, acc, x.ring_a + slot1 * (uint32_t)p.slot_bytes,
-                                                     (ks + 1) * rows, sum_base);
-        }
+        if (!x.aborted)
+            stage_math2<MT, SIGNED, HAS_ZP, FB8, KIND>(p, lo, acc, x.ring_a + slot * (uint32_t)p.slot_bytes,
+                                                      x.ring_a + slot1 * (uint32_t)p.slot_bytes, ks * rows,
+                                                      (ks + 1) * rows, sum_base);
         // every lane's reads of both slots are complete (their results fed
         // the MMAs above): release them to the producer
         __syncwarp();

@@ -54,8 +54,9 @@ int t4b_last_cuda_error(void);
 int t4b_version(void);
 
 /* Reads (and, if `clear`, resets) the library's device error words on the
- * current device -- the decode GEMV's and the prefill GEMM's (one each per
- * device), the allocation-free GEMV's (in its fixed scratch array) and the one
+ * current device -- the decode GEMV's, the prefill GEMM's and the INT3 GEMV's
+ * (one each per device), the allocation-free GEMV's (in its fixed scratch
+ * array) and the one
  * in the workspace kept for `stream` (if any), ORed: bit 0 = a kernel gave up
  * a bounded wait (its output is then invalid).  Synchronizes `stream`; do not
  * call while the stream is being captured.  No counterpart in the reference,
@@ -81,6 +82,13 @@ enum {
 /* Sets the process-wide choice; returns the previous one (-1: bad argument).
  * No counterpart in the reference (it has a single kernel). */
 int t4b_set_gemv_kernel(int which);
+
+/* Kernel choice for the INT3 GEMV: 0 = the register-streaming kernel (the
+ * default); 1 = the warp-specialized TMA-ring kernel where it applies
+ * (N % 4 == 0, W 16-byte and scales 8-byte aligned), else register streaming.
+ * Returns the previous choice (-1: bad argument).  No counterpart in the
+ * reference. */
+int t4b_set_int3_kernel(int which);
 
 /* ---- flat dequantization ----------------------------------------------
  * out[8*i + j] = dequant(nibble j of words[i], scales[i], zero_points[i]).

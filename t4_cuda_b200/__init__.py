@@ -18,6 +18,7 @@ from .ops import (  # noqa: F401
     fused_w4a16_gemm_s4,
     fused_h17_gemv_s3,
     set_gemv_kernel,
+    set_int3_kernel,
     device_error,
 )
 from ._lib import LIB_PATH, T4BError, load as load_library  # noqa: F401

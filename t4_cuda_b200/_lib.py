@@ -80,6 +80,8 @@ def load():
         lib.t4b_version.restype = ctypes.c_int
         lib.t4b_set_gemv_kernel.argtypes = [ctypes.c_int]
         lib.t4b_set_gemv_kernel.restype = ctypes.c_int
+        lib.t4b_set_int3_kernel.argtypes = [ctypes.c_int]
+        lib.t4b_set_int3_kernel.restype = ctypes.c_int
         lib.t4b_device_error.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
         lib.t4b_device_error.restype = ctypes.c_int
         lib.t4b_workspace_bytes.argtypes = [_vp, ctypes.POINTER(ctypes.c_size_t)]

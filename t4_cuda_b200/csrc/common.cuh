@@ -59,6 +59,8 @@ int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const vo
 int decode_device_error(cudaStream_t stream, unsigned* out, bool clear);
 // Same for the allocation-free GEMV's word (in its fixed scratch array).
 int static_scratch_error(cudaStream_t stream, unsigned* out, bool clear);
+// Same for the TMA-ring INT3 GEMV's word.
+int int3_device_error(cudaStream_t stream, unsigned* out, bool clear);
 
 // Prefill GEMM on tcgen05 / TMEM (M > 16, K % 64 == 0, group % 64 == 0);
 // T4B_ERR_UNSUPPORTED (without launching) for shapes it does not take.

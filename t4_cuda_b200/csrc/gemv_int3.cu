@@ -15,7 +15,9 @@
 //    10*kw .. 10*kw+9 crosses a multiple of 128) each pair picks its scale and
 //    zero point per element; otherwise one scale serves the whole word.
 #include "common.cuh"
+#include "tma.cuh"
 
+#include <atomic>
 #include <cooperative_groups.h>
 
 namespace cg = cooperative_groups;
@@ -24,6 +26,15 @@ namespace t4b {
 namespace {
 
 constexpr int kWarps = 8;
+
+// 0: register streaming (the default); 1: the warp-specialized TMA-ring form
+// where it applies.  The ring form is correct and tested but slower on every
+// benchmarked shape (14340 x 14336: 99 against 63 us): the step math -- ~9
+// integer and ~10 fp16 operations per 10-weight word for the exact contract
+// dequant with per-element group selection -- bounds this kernel, not the
+// weight stream, and the register-streaming form keeps more steps in flight
+// per SM (16 warps with two steps each against 8 warps with one).
+std::atomic<int> g_int3_kernel{0};
 constexpr int kTileN = 64;
 constexpr int kNB = 2;
 
@@ -310,6 +321,329 @@ gemv_int3_kernel(const Int3Params p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-specialized TMA-ring form (selected by t4b_set_int3_kernel).  The same
+// step math as above, but the words reach the math warps through a ring of
+// shared-memory stages that one producer warp fills with TMA: every stage the
+// ring holds is requested at kernel entry, before griddepcontrol.wait, so the
+// weight stream of a CTA's K range is in flight while the previous kernel
+// drains, and a math warp's step waits on shared memory (~30 cycles), not on
+// HBM.  A stage is 64 word rows (one 8-row step per math warp) of the CTA's 64
+// columns, two 32-column boxes with 128-byte swizzle: lane (r, c) reads rows
+// 2c and 2c + 1 of its warp's 8 at 16-byte unit r ^ (row & 7), which puts the
+// 8 lanes of every quarter-warp on 8 distinct bank groups.  Scales, zero points
+// and activations are read as in the register-streaming form (they are small
+// and cached).  K is split over a cluster exactly as there.
+namespace ring {
+
+constexpr int kRows = 8 * kWarps;                       // word rows per stage
+constexpr int kBoxCols = 32;                            // 128-byte box rows
+constexpr int kStageBytes = kRows * kTileN * 4;         // 16 KB
+constexpr int kMaxStages = 12;
+constexpr int kThreads = (kWarps + 1) * 32;             // + one producer warp
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr unsigned kErrTimeout = 1u;
+
+// Device error word of the ring form (bit 0: a bounded wait gave up).
+__device__ unsigned g_int3_error = 0;
+
+struct RingParams {
+    int stages;           // ring depth
+    int rows_per_split;   // word rows of one K split (a multiple of 8)
+    int total_steps;      // 8-row steps of the whole K (ceil(KW / 8))
+};
+
+// The words of `step` (8-row step of the whole K) for this lane from ring
+// slot `slot_a` (row 8 * warp + 2c + e of the stage), plus its scales, zero
+// points and activations as load_step reads them.
+template <int MT, bool HAS_ZP>
+__device__ __forceinline__ void load_step_smem(const Int3Params& p, Int3Step<MT, HAS_ZP>& d, uint32_t slot_a, int step,
+                                               bool in_range, int warp, int r, int c, int n0, int m0) {
+    const int kwb = 8 * step + 2 * c;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const int kw = kwb + e;
+        const bool vk = in_range && kw < p.KW;
+        const int k0 = 10 * kw;
+        const int g = vk ? (int)fdiv((uint32_t)k0, p.gdiv) : 0;
+        const int split = (g + 1) * p.group - k0;          // elements >= split use group g + 1
+        const bool straddle = vk && split < 10;
+        d.split[e] = straddle ? split : 10;
+        const int row = 8 * warp + 2 * c + e;              // row within the stage
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int col = n0 + 32 * h + 4 * r;
+            const bool v = vk && col < p.N;
+            uint4 wv = make_uint4(0, 0, 0, 0);
+            if (vk) {
+                const uint32_t a = slot_a + (uint32_t)(h * (kRows * 128) + row * 128) + (uint32_t)((r ^ (row & 7)) << 4);
+                asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w) : "r"(a) : "memory");
+            }
+            d.w[e][4 * h + 0] = wv.x; d.w[e][4 * h + 1] = wv.y; d.w[e][4 * h + 2] = wv.z; d.w[e][4 * h + 3] = wv.w;
+            load_row4<true>(p.S, (size_t)g * p.N + col, col, p.N, v, d.slo[e][2 * h], d.slo[e][2 * h + 1]);
+            load_row4<true>(p.S, (size_t)(g + 1) * p.N + col, col, p.N, v && straddle, d.shi[e][2 * h], d.shi[e][2 * h + 1]);
+            if constexpr (HAS_ZP) {
+                load_row4<true>(p.Z, (size_t)g * p.N + col, col, p.N, v, d.zlo[e][2 * h], d.zlo[e][2 * h + 1]);
+                load_row4<true>(p.Z, (size_t)(g + 1) * p.N + col, col, p.N, v && straddle, d.zhi[e][2 * h],
+                                d.zhi[e][2 * h + 1]);
+            }
+        }
+    }
+    const bool vk0 = in_range && kwb < p.KW;
+    const bool vk1 = in_range && kwb + 1 < p.KW;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        const int m = m0 + 8 * mt + r;
+        const uint16_t* src = p.A + (size_t)m * p.K + 10 * kwb;
+        const bool vm = m < p.M;
+        if (p.a_vec8) {
+#pragma unroll
+            for (int q = 0; q < 5; ++q) {
+                uint32_t lo = 0u, hi = 0u;
+                if (q == 2) {
+                    if (vm && vk1) {
+                        const uint2 t = __ldcg(reinterpret_cast<const uint2*>(src) + q);
+                        lo = t.x; hi = t.y;
+                    } else if (vm && vk0) {
+                        lo = __ldcg(reinterpret_cast<const uint32_t*>(src) + 4);
+                    }
+                } else if (vm && (q < 2 ? vk0 : vk1)) {
+                    const uint2 t = __ldcg(reinterpret_cast<const uint2*>(src) + q);
+                    lo = t.x; hi = t.y;
+                }
+                d.a[mt][2 * q] = lo; d.a[mt][2 * q + 1] = hi;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 10; ++q) {
+                const bool v = vm && (q < 5 ? vk0 : vk1);
+                d.a[mt][q] = v ? __ldcg(reinterpret_cast<const uint32_t*>(src) + q) : 0u;
+            }
+        }
+    }
+}
+
+template <int MT, bool HAS_ZP, bool CLUSTER>
+__global__ void __launch_bounds__(kThreads, 1)
+gemv_int3_ring_kernel(const __grid_constant__ CUtensorMap wmap, const Int3Params p, const RingParams rp) {
+    constexpr int MR = 8 * MT;
+    constexpr int RED_STRIDE = MR + 1;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    float* red = reinterpret_cast<float*>(ring + (size_t)rp.stages * kStageBytes);   // [kWarps][kTileN * RED_STRIDE]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + kWarps * kTileN * RED_STRIDE);
+    uint64_t* empty = full + kMaxStages;
+    volatile int* sflag = reinterpret_cast<volatile int*>(empty + kMaxStages);   // [0] abort, [1] stages issued
+
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n0 = blockIdx.x * kTileN;
+    const int m0 = blockIdx.z * MR;
+    const int kb = blockIdx.y * rp.rows_per_split;                 // first word row of this split
+    const int ke = min(p.KW, kb + rp.rows_per_split);
+    const int nst = ke > kb ? (ke - kb + kRows - 1) / kRows : 0;   // stages of this CTA
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < rp.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        sflag[0] = 0;
+        sflag[1] = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    float acc[MT][4][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[mt][t][i] = 0.f;
+
+    if (warp == kWarps) {
+        // ---------------- producer: every stage the ring holds before the
+        // dependency wait (the words are never written by a kernel of this
+        // library), then refills as the math warps release slots
+        if (lane == 0) {
+            prefetch_tmap(&wmap);
+            auto issue = [&](int i, int slot) {
+                uint8_t* dst = ring + (size_t)slot * kStageBytes;
+                mbar_arrive_expect_tx(&full[slot], (uint32_t)kStageBytes);
+                tma_load_2d(dst, &wmap, n0, kb + i * kRows, &full[slot]);
+                tma_load_2d(dst + kRows * 128, &wmap, n0 + kBoxCols, kb + i * kRows, &full[slot]);
+            };
+            const int early = nst < rp.stages ? nst : rp.stages;
+            for (int i = 0; i < early; ++i) issue(i, i);
+            sflag[1] = early;
+            bool ok = true;
+            for (int i = early; i < nst; ++i) {
+                const int slot = i % rp.stages;
+                if (!mbar_wait_bounded(&empty[slot], (uint32_t)(((i / rp.stages) & 1) ^ 1), kWaitLimitNs)) {
+                    ok = false;
+                    break;
+                }
+                if (sflag[0]) break;
+                fence_proxy_async_smem();    // the math warps' reads of the slot before the copy overwrites it
+                issue(i, slot);
+                sflag[1] = i + 1;
+            }
+            if (!ok) {
+                sflag[0] = 1;
+                atomicOr(&g_int3_error, kErrTimeout);
+            }
+        }
+    } else {
+        // ---------------- math warps: one 8-row step per stage each
+        const int r = lane >> 2, c = lane & 3;
+        pdl_wait_prior_grid();       // A may belong to the previous kernel
+        const uint32_t ring_a = smem_addr(ring);
+        bool aborted = false;
+        Int3Step<MT, HAS_ZP> d;
+        for (int i = 0; i < nst; ++i) {
+            const int slot = i % rp.stages;
+            if (!aborted && sflag[0]) aborted = true;      // the producer gave up: nothing more lands
+            if (!aborted && !mbar_wait_bounded(&full[slot], (uint32_t)((i / rp.stages) & 1), kWaitLimitNs)) {
+                aborted = true;
+                sflag[0] = 1;
+                atomicOr(&g_int3_error, kErrTimeout);
+            }
+            const int step = (kb >> 3) + i * kWarps + warp;
+            const bool in_range = !aborted && 8 * step < ke;
+            load_step_smem<MT, HAS_ZP>(p, d, ring_a + (uint32_t)slot * kStageBytes, step, in_range, warp, r, c, n0, m0);
+            // the slot's words are in registers: release it before the math
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (in_range) compute_step<MT, HAS_ZP>(d, acc);
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int c0 = slot_col(r, 2 * t), c1 = slot_col(r, 2 * t + 1);
+                const int mm = 8 * mt + 2 * c;
+                float* rw = red + warp * (kTileN * RED_STRIDE);
+                rw[c0 * RED_STRIDE + mm] = acc[mt][t][0];
+                rw[c0 * RED_STRIDE + mm + 1] = acc[mt][t][1];
+                rw[c1 * RED_STRIDE + mm] = acc[mt][t][2];
+                rw[c1 * RED_STRIDE + mm + 1] = acc[mt][t][3];
+            }
+    }
+    __syncthreads();
+    if (sflag[0] && threadIdx.x == 0) {
+        // do not leave while copies may still be landing in this CTA's memory
+        const int issued = sflag[1];
+        for (int j = (issued > rp.stages ? issued - rp.stages : 0); j < issued; ++j)
+            mbar_wait_bounded(&full[j % rp.stages], (uint32_t)((j / rp.stages) & 1), kWaitLimitNs / 4);
+    }
+    constexpr int OUTS = kTileN * MR;
+    for (int o = threadIdx.x; o < OUTS; o += kThreads) {
+        const int idx = (o / MR) * RED_STRIDE + (o % MR);
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += red[w * (kTileN * RED_STRIDE) + idx];
+        red[idx] = v;
+    }
+    if constexpr (CLUSTER) {
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        const int nranks = (int)cluster.num_blocks();
+        const int rank = (int)cluster.block_rank();
+        const int per = (OUTS + nranks - 1) / nranks;
+        const int o_end = min(OUTS, (rank + 1) * per);
+        for (int o = rank * per + threadIdx.x; o < o_end; o += kThreads) {
+            const int col = o / MR, mm = o % MR;
+            const int idx = col * RED_STRIDE + mm;
+            float v = 0.f;
+            for (int q = 0; q < nranks; ++q) v += cluster.map_shared_rank(red, q)[idx];
+            const int m = m0 + mm, n = n0 + col;
+            if (m < p.M && n < p.N) p.C[(size_t)m * p.N + n] = __half_as_ushort(__float2half_rn(v));
+        }
+        cluster.sync();
+    } else {
+        __syncthreads();
+        for (int o = threadIdx.x; o < OUTS; o += kThreads) {
+            const int col = o / MR, mm = o % MR;
+            const int m = m0 + mm, n = n0 + col;
+            if (m < p.M && n < p.N) p.C[(size_t)m * p.N + n] = __half_as_ushort(__float2half_rn(red[col * RED_STRIDE + mm]));
+        }
+    }
+}
+
+template <int MT, bool HAS_ZP>
+int launch(const CUtensorMap& wmap, const Int3Params& p, const RingParams& rp, int splits, size_t smem,
+           cudaStream_t stream) {
+    auto kern = splits > 1 ? gemv_int3_ring_kernel<MT, HAS_ZP, true> : gemv_int3_ring_kernel<MT, HAS_ZP, false>;
+    static SmemLimit limit[2];     // per instantiation (cluster or not), per device
+    const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit[splits > 1 ? 1 : 0]);
+    if (st != T4B_OK) return st;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p.N + kTileN - 1) / kTileN, splits, (p.M + 8 * MT - 1) / (8 * MT));
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+    if (splits > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = 1;
+        attr[n].val.clusterDim.y = splits;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, wmap, p, rp);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    return T4B_OK;
+}
+
+// T4B_ERR_UNSUPPORTED (nothing launched) where the ring form does not apply.
+int fused_int3_ring(const Int3Params& p, const void* W, cudaStream_t stream) {
+    if ((p.N % 4) != 0 || !aligned(W, 16) || !aligned(p.S, 8) || (p.Z && !aligned(p.Z, 8))) return T4B_ERR_UNSUPPORTED;
+    const int mt = (p.M <= 8) ? 1 : 2;
+    const int tiles = (p.N + kTileN - 1) / kTileN;
+    const int chunks = (p.M + 8 * mt - 1) / (8 * mt);
+    // split K over a cluster until the CTAs cover the SMs, at most 8 ways, and
+    // at least one stage each
+    int splits = sm_count() / (tiles * chunks);
+    if (splits > 8) splits = 8;
+    while (splits > 1 && splits * kRows > p.KW) --splits;
+    if (splits < 1) splits = 1;
+    while (splits > 1 && (splits & (splits - 1))) --splits;   // cluster sizes 1, 2, 4, 8
+    RingParams rp;
+    rp.total_steps = (p.KW + 7) / 8;
+    rp.rows_per_split = 8 * ((rp.total_steps + splits - 1) / splits);
+    const size_t red_bytes = (size_t)kWarps * kTileN * (8 * mt + 1) * 4;
+    const size_t fixed = 1024 + red_bytes + 2 * kMaxStages * 8 + 16;
+    int optin = 0, per_sm = 0, reserved = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    // more CTAs than SMs (wide N): a ring half the size so that two CTAs share
+    // an SM and the grid runs as one wave
+    const bool two_per_sm = tiles * chunks * splits > sm_count();
+    const size_t budget = two_per_sm ? (size_t)(per_sm / 2 - reserved) : (size_t)optin;
+    int stages = budget > fixed ? (int)((budget - fixed) / kStageBytes) : 0;
+    if (stages > kMaxStages) stages = kMaxStages;
+    if (stages < 2) return T4B_ERR_UNSUPPORTED;
+    rp.stages = stages;
+    const size_t smem = fixed + (size_t)stages * kStageBytes;
+    CUtensorMap wmap;
+    if (!make_tmap_2d_ex(&wmap, false, W, (uint64_t)p.KW, (uint64_t)p.N, kRows, kBoxCols, 128, 256))
+        return T4B_ERR_UNSUPPORTED;
+    const bool zp = p.Z != nullptr;
+    if (mt == 1) return zp ? launch<1, true>(wmap, p, rp, splits, smem, stream) : launch<1, false>(wmap, p, rp, splits, smem, stream);
+    return zp ? launch<2, true>(wmap, p, rp, splits, smem, stream) : launch<2, false>(wmap, p, rp, splits, smem, stream);
+}
+
+}  // namespace ring
+
 template <int MT, bool HAS_ZP, bool VEC>
 int launch(const Int3Params& p, int splits, cudaStream_t stream) {
     const dim3 block(kWarps * 32);
@@ -359,6 +693,11 @@ int fused_int3(const void* A, const void* W, const void* S, const void* Z, void*
     p.gdiv = make_fastdiv((uint32_t)group);
     p.total_steps = (p.KW + 7) / 8;
     p.a_vec8 = (K % 4 == 0) ? 1 : 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream_);
+    if (g_int3_kernel.load() == 1) {
+        const int st = ring::fused_int3_ring(p, W, s);
+        if (st != T4B_ERR_UNSUPPORTED) return st;
+    }
     const bool vec = (N % 4 == 0) && aligned(W, 16) && aligned(S, 8) && (!Z || aligned(Z, 8));
     const int mt = (M <= 8) ? 1 : 2;
     const int tiles = (N + kTileN - 1) / kTileN;
@@ -372,13 +711,27 @@ int fused_int3(const void* A, const void* W, const void* S, const void* Z, void*
     if (splits < 1) splits = 1;
     const int warps = splits * kWarps;
     p.steps_per_warp = (p.total_steps + warps - 1) / warps;
-    cudaStream_t s = static_cast<cudaStream_t>(stream_);
     if (mt == 1) return Z ? dispatch_vec<1, true>(p, vec, splits, s) : dispatch_vec<1, false>(p, vec, splits, s);
     return Z ? dispatch_vec<2, true>(p, vec, splits, s) : dispatch_vec<2, false>(p, vec, splits, s);
 }
 
 }  // namespace
+
+int int3_device_error(cudaStream_t stream, unsigned* out, bool clear) {
+    unsigned* word = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&word), ring::g_int3_error);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, word, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(word, 0, sizeof(unsigned), stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e == cudaSuccess ? T4B_OK : record_cuda_error(e);
+}
+
 }  // namespace t4b
+
+extern "C" int t4b_set_int3_kernel(int which) {
+    if (which < 0 || which > 1) return -1;
+    return t4b::g_int3_kernel.exchange(which);
+}
 
 extern "C" int t4b_fused_h17_gemv_s3(const void* A, const void* W_packed, const void* scales,
                                      const void* zero_points, void* C, int M, int N, int K, int group_size,

@@ -43,6 +43,18 @@ def set_gemv_kernel(which="auto"):
     return {v: k for k, v in _GEMV_KERNELS.items()}[prev]
 
 
+_INT3_KERNELS = {"stream": 0, "ring": 1}
+
+
+def set_int3_kernel(which="stream"):
+    """Choose the INT3 GEMV kernel process-wide: "stream" (the register-streaming
+    kernel, the default) or "ring" (the warp-specialized TMA-ring kernel where it
+    applies, else register streaming).  Returns the previous choice."""
+    _check(which in _INT3_KERNELS, f"which must be one of {sorted(_INT3_KERNELS)}")
+    prev = _lib.load().t4b_set_int3_kernel(_INT3_KERNELS[which])
+    return {v: k for k, v in _INT3_KERNELS.items()}[prev]
+
+
 def device_error(device=None, clear=True):
     """Device error word of this library's workspace for the current stream of
     ``device`` (0 = no kernel gave up a bounded wait).  Synchronizes the stream."""

@@ -9,6 +9,7 @@ import pytest
 import torch
 
 import oracle
+import t4_cuda_b200
 import t4_kernels
 from tests.conftest import GOLDEN
 from tests.test_gemv_gpu import assert_gemm_close
@@ -48,6 +49,16 @@ def make_int3(rng, M, K, N, group, zp):
     return A, W, s, z
 
 
+@pytest.fixture(params=["stream", "ring"])
+def int3_kernel(request, cuda_device):
+    """Both INT3 kernels: the register-streaming one (the default) and the
+    warp-specialized TMA-ring one."""
+    prev = t4_cuda_b200.set_int3_kernel(request.param)
+    yield request.param
+    t4_cuda_b200.set_int3_kernel(prev)
+    assert t4_cuda_b200.device_error(cuda_device) == 0
+
+
 @pytest.mark.parametrize("M,K,N,group,zp", [
     (1, 4100, 4096, 128, False),     # Llama K=4096 padded to a multiple of 10, group 128
     (1, 4100, 1024, 100, True),
@@ -58,7 +69,7 @@ def make_int3(rng, M, K, N, group, zp):
     (2, 10, 8, 100, True),           # one word row; K % 4 != 0 activation path
     (20, 1000, 72, 13, True),        # odd group size, M > 16
 ])
-def test_int3_vs_oracle(cuda_device, M, K, N, group, zp):
+def test_int3_vs_oracle(cuda_device, int3_kernel, M, K, N, group, zp):
     rng = np.random.default_rng(abs(hash((M, K, N, group, zp))) % 2 ** 32)
     A, W, s, z = make_int3(rng, M, K, N, group, zp)
     zt = _dev(z, cuda_device) if zp else torch.empty(0, dtype=torch.float16, device=cuda_device)
@@ -92,3 +103,27 @@ def test_checks_mirror_the_reference(cuda_device):
                                      group_size=7)
     with pytest.raises(RuntimeError, match="contiguous"):
         t4_kernels.fused_h17_gemv_s3(A, W.t().contiguous().t(), s, s)
+
+
+@pytest.mark.parametrize("group", [128, 100])
+@pytest.mark.parametrize("K,N", [(4100, 4096), (4100, 14336), (14340, 4096), (14340, 14336)])
+def test_int3_benchmark_configs(cuda_device, int3_kernel, K, N, group):
+    """The INT3 configuration the benchmark reports (M = 1, K in {4096, 14336}
+    padded to 4100 / 14340, N in {4096, 14336}) at full size on the GPU; the
+    oracle checks a fixed random subset of columns (columns are independent):
+    every 64-column block contributes two, plus the first and last."""
+    rng = np.random.default_rng(K + N + group)
+    A = rng.standard_normal((1, K), dtype=np.float32).astype(np.float16)
+    W = rng.integers(0, 2 ** 30, size=(K // 10, N), dtype=np.uint32).view(np.int32)
+    G = (K + group - 1) // group
+    s = (np.abs(rng.standard_normal((G, N), dtype=np.float32)) * 0.02 + 1e-3).astype(np.float16)
+    C = t4_kernels.fused_h17_gemv_s3(_dev(A, cuda_device), _dev(W, cuda_device), _dev(s, cuda_device),
+                                     torch.empty(0, dtype=torch.float16, device=cuda_device), group_size=group)
+    assert bool(torch.isfinite(C).all())
+    cols = {0, N - 1}
+    for b0 in range(0, N, 64):
+        cols.update(rng.choice(np.arange(b0, min(N, b0 + 64)), size=2, replace=False).tolist())
+    cols = np.array(sorted(cols))
+    ref = oracle.ref_int3_gemv(A, W[:, cols], s[:, cols], None, group)
+    y = C[:, torch.from_numpy(cols).to(cuda_device)]
+    assert_gemm_close(y, ref, f"{int3_kernel}: K={K} N={N} g={group} ({len(cols)} columns checked)")

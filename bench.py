@@ -70,6 +70,19 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+def load_gemm_traffic():
+    """DRAM bytes of one prefill GEMM launch (M = K = N = 4096) from the committed
+    ncu summary (profiles/gemm_w4_tc_pair_4096.md, line
+    'traffic_bytes_per_launch <name> <bytes>')."""
+    p = os.path.join(ROOT, "profiles", "gemm_w4_tc_pair_4096.md")
+    if os.path.exists(p):
+        for line in open(p):
+            parts = line.strip().strip("`").split()
+            if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch":
+                return float(parts[2])
+    return None
+
+
 def load_traffic():
     """DRAM bytes of one decode step from the committed ncu summary
     (profiles/gemv_w4_decode.md, line 'traffic_bytes_per_step <name> <bytes>');
@@ -328,6 +341,14 @@ def decode_batch(dev, Ms=(1, 4, 8, 16), reps=10):
     return out
 
 
+def _pct(sorted_vals, q):
+    """q-th percentile (nearest rank) of an ascending list."""
+    if not sorted_vals:
+        return float("nan")
+    k = max(0, min(len(sorted_vals) - 1, int(round(q / 100.0 * (len(sorted_vals) - 1)))))
+    return sorted_vals[k]
+
+
 def _max_over_ranks(dist, dev, ms):
     if dist is None:
         return ms
@@ -538,15 +559,17 @@ def run_ours(args):
     for _ in range(args.warmup):
         run_step()
     barrier_sync()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # one event between consecutive steps: the whole region and every step
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(local) as clk:
-        start.record()
-        for _ in range(args.steps):
+        evs[0].record()
+        for i in range(args.steps):
             run_step()
-        end.record()
-        end.synchronize()
+            evs[i + 1].record()
+        evs[-1].synchronize()
     barrier_sync()
-    ms = start.elapsed_time(end)
+    ms = evs[0].elapsed_time(evs[-1])
+    step_ms = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps))
     if dist is not None:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -666,7 +689,10 @@ def run_ours(args):
                 "note": "timed region holds only gemv_w4_decode_kernel launches; duration per launch = region / launches"}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "step_ms_rank0": {"median": round(_pct(step_ms, 50), 4), "p5": round(_pct(step_ms, 5), 4),
+                          "p95": round(_pct(step_ms, 95), 4)},
+        "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16 (int4 weights, fp32 accumulate)",
         "data": "synthetic",
         "config": {"workload": WORKLOAD,
@@ -696,7 +722,10 @@ def run_ours(args):
         gemm["roofline"] = {"bound": "tensor", "achieved": gemm["value"], "peak": pk, "unit": "TFLOP/s",
                             "frac": round(gemm["value"] / pk, 4),
                             "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)" if peaks["source"] == "measured"
-                            else "fallback 1590 TFLOP/s", "traffic": None}
+                            else "fallback 1590 TFLOP/s", "traffic": load_gemm_traffic(),
+                            "traffic_note": "DRAM bytes of one 4096 x 4096 x 4096 launch (ncu, "
+                                            "profiles/gemm_w4_tc_pair_4096.md); the seven projections differ in shape",
+                            "timing": "CUDA events around 5 eager steps on one fixed weight set (compute-bound)"}
         line["gemm"] = gemm
     if others is not None:
         line["other_kernels"] = others

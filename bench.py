@@ -21,7 +21,8 @@ The line also carries "decode_batch" (one GPU): the four projection shapes
 at M in {1, 4, 8, 16}, one launch at a time; "gemm_sweep" (one GPU): the
 same shapes at M in {512, 2048, 4096} on the tcgen05 GEMM; and
 "sharded_70b": Llama-3-70B layer projections column-sharded over the same
-N GPUs at M in {1, 16, 256, 4096} (see sharded_70b).
+N GPUs at M in {1, 16, 256, 4096} (see sharded_70b); "fp8_gemm" (one GPU): the
+FP8-E4M3 weight GEMM at the four shapes, M = 1 and M = 4096.
 
 --impl reference times the reference's CPU dequant + matmul path
 (tests/test_fused_gemm_correctness.py:22-36, restated in oracle/cpu_path.py)
@@ -279,6 +280,32 @@ def int3_and_dequant(dev):
         us = _graph_us(dev, calls)
         out["dequant"][kind] = {"words": words, "us": round(us, 3), "GB/s": round(byts / us / 1e3, 1)}
         del Ws
+    return out
+
+
+def fp8_gemm(dev, reps=5):
+    """The FP8-E4M3 weight GEMM (tcgen05, E4M3 -> fp16 dequant stage) at the
+    Llama-3-8B projection shapes: M = 1 (decode; weights rotate through a pool
+    >= 4x L2; GB/s of algorithmic bytes K N + (K/128) N 2 + 2 M K + 2 M N) and
+    M = 4096 (prefill; TFLOP/s = 2 M K N), each a CUDA graph, CUDA events."""
+    from t4_cuda_b200 import ops
+    gen = torch.Generator(device=dev).manual_seed(13)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    out = {"decode_M=1": {}, "prefill_M=4096": {}}
+    for K, N in ((4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)):
+        pool = max(2, math.ceil(4 * l2 / (K * N)))
+        # random E4M3 codes without the two NaN codes (0x7F, 0xFF)
+        Ws = [(torch.randint(0, 2 ** 31 - 1, (K // 4, N), dtype=torch.int32, device=dev, generator=gen)
+               & 0x7E7E7E7E) for _ in range(pool)]
+        S = (torch.randn((K // GROUP, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+        A1 = torch.randn((1, K), device=dev, generator=gen).half()
+        us = _graph_us(dev, [lambda W=W: ops.fused_w8a16_gemm_fp8(A1, W, S) for W in Ws])
+        byts = K * N + (K // GROUP) * N * 2 + K * 2 + N * 2
+        out["decode_M=1"][f"{K}x{N}"] = {"us": round(us, 3), "GB/s": round(byts / us / 1e3, 1)}
+        A4 = torch.randn((4096, K), device=dev, generator=gen).half()
+        us = _graph_us(dev, [lambda: ops.fused_w8a16_gemm_fp8(A4, Ws[0], S)] * reps, reps=4)
+        out["prefill_M=4096"][f"{K}x{N}"] = {"us": round(us, 2), "TFLOP/s": round(2.0 * 4096 * K * N / us / 1e6, 1)}
+        del Ws, A4
     return out
 
 
@@ -609,6 +636,7 @@ def run_ours(args):
         others = int3_and_dequant(dev)
     batch = decode_batch(dev) if world == 1 else None
     sweep = gemm_sweep(dev) if world == 1 and not args.no_gemm else None
+    fp8 = fp8_gemm(dev) if world == 1 and not args.no_gemm else None
 
     # ---- end to end through the public API, host buffers, copies timed
     pin = {a: t.cpu().pin_memory() for a, t in acts.items()}
@@ -733,6 +761,8 @@ def run_ours(args):
         line["decode_batch"] = batch
     if sweep is not None:
         line["gemm_sweep"] = sweep
+    if fp8 is not None:
+        line["fp8_gemm"] = fp8
     if sh70 is not None:
         line["sharded_70b"] = sh70
     if world == 1 and not args.no_cpu_baseline:

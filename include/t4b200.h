@@ -137,6 +137,18 @@ int t4b_fused_w4a16_gemm_s4(const void* A, const void* W_packed, const void* sca
                             const void* zero_points, void* C, int M, int N, int K,
                             int group_size, void* stream);
 
+/* FP8-E4M3 weight GEMM.  No counterpart in the reference, which has only the
+ * flat dequantizer of this format (launch_lop3_dequant_fp8,
+ * src/kernels/lop3_dequant.h:135-136): the fused path for it.
+ * C[M, N] (f16) = A[M, K] (f16) x (E4M3(W) * s)[K, N]; W_packed int32 [K/4, N],
+ * byte j of word (kw, n) = K row 4 kw + j; scales f16 [K/group_size, N].  The
+ * weight is f16(e4m3 * s) with exact E4M3 decoding (subnormals are values,
+ * 0x7F / 0xFF are NaN); products and sums fp32.  Runs the tcgen05 GEMM for any
+ * M >= 1; needs K % 64 == 0, group_size % 64 == 0, N % 8 == 0 and 16-byte
+ * aligned pointers (else T4B_ERR_UNSUPPORTED / T4B_ERR_MISALIGNED). */
+int t4b_fused_w8a16_gemm_fp8(const void* A, const void* W_packed, const void* scales, void* C,
+                             int M, int N, int K, int group_size, void* stream);
+
 /* Allocation-free decode GEMV.  No counterpart in the reference: an addition
  * for callers that cannot allocate device memory while they run -- a serving
  * engine that reserves all of HBM for its own pool at start-up, or a host

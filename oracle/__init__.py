@@ -40,3 +40,10 @@ from .int3 import (  # noqa: F401
     dequant_int3_matrix,
     ref_int3_gemv,
 )
+from .fp8 import (  # noqa: F401
+    e4m3_to_float,
+    pack_fp8,
+    unpack_fp8_codes,
+    dequant_fp8_matrix,
+    ref_fp8_gemm,
+)

@@ -23,6 +23,7 @@ SIGNATURES = {
     "t4b_fused_w4a16_gemm_u4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_w4a16_gemm_s4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_h17_gemv_s3": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
+    "t4b_fused_w8a16_gemm_fp8": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_w4a16_gemv_noalloc": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_w4a16_gemv_allgather": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp],
     "t4b_fused_w4a16_gemv_allgather_supported": [_i32, _i32, _i32, _i32, _i32],

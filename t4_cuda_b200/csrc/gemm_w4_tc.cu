@@ -151,16 +151,37 @@ __device__ __forceinline__ void unpack_natural(uint32_t w, uint32_t (&q)[4]) {
     }
 }
 
-template <bool SIGNED, bool HAS_ZP>
+// Per weight format of the single-CTA kernel: INT4 packs 8 K values in a word
+// (8 word rows per K step of 64), FP8-E4M3 4 (16 word rows, a twice larger
+// packed tile, so one TMA stage fewer fits in shared memory).
+template <bool FP8>
+struct TcCfg {
+    static constexpr int kWordRows = FP8 ? kBK / 4 : kBK / 8;
+    static constexpr int kWBytes = kWordRows * kBN * 4;
+    static constexpr int kTmaStages = FP8 ? 4 : 5;
+    static constexpr int kTmaStageBytes = kABytes + kWBytes + 2 * kSBytes;
+    static constexpr int kRingBytes = kTmaStages * kTmaStageBytes + kBStages * kBBytes;
+    static constexpr int kBarriers = 2 * kTmaStages + 2 * kBStages + 1;
+};
+
+// Two E4M3 bytes (low byte first) -> fp16x2 (low half first), exactly.
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint16_t v) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(v));
+    return d;
+}
+
+template <bool SIGNED, bool HAS_ZP, bool FP8>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+    using C = TcCfg<FP8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    // TMA slot s: [A 16 KB][packed 8 KB][scales 512][zero points 512]; then the B slots (32 KB each)
-    uint8_t* bring = base + kTmaStages * kTmaStageBytes;
-    uint64_t* full_tma = reinterpret_cast<uint64_t*>(base + kRingBytes);
-    uint64_t* empty_tma = full_tma + kTmaStages;
-    uint64_t* full_b = empty_tma + kTmaStages;
+    // TMA slot s: [A 16 KB][packed 8 KB (fp8: 16 KB)][scales 512][zero points 512]; then the B slots (32 KB each)
+    uint8_t* bring = base + C::kTmaStages * C::kTmaStageBytes;
+    uint64_t* full_tma = reinterpret_cast<uint64_t*>(base + C::kRingBytes);
+    uint64_t* empty_tma = full_tma + C::kTmaStages;
+    uint64_t* full_b = empty_tma + C::kTmaStages;
     uint64_t* empty_b = full_b + kBStages;
     uint64_t* acc_full = empty_b + kBStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
@@ -173,7 +194,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     volatile int* last_flag = abort_flag + 1;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTmaStages; ++s) {
+        for (int s = 0; s < C::kTmaStages; ++s) {
             mbar_init(&full_tma[s], 1);
             mbar_init(&empty_tma[s], 1);          // tcgen05.commit
         }
@@ -203,18 +224,18 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         // ---------------- TMA producer
         if (lane == 0) {
             for (int i = 0; i < nsteps; ++i) {
-                const int s = i % kTmaStages;
-                const uint32_t ph = (uint32_t)((i / kTmaStages) & 1);
-                if (i >= kTmaStages && !wait_or_abort(&empty_tma[s], ph ^ 1u, abort_flag)) break;
-                uint8_t* st = base + s * kTmaStageBytes;
+                const int s = i % C::kTmaStages;
+                const uint32_t ph = (uint32_t)((i / C::kTmaStages) & 1);
+                if (i >= C::kTmaStages && !wait_or_abort(&empty_tma[s], ph ^ 1u, abort_flag)) break;
+                uint8_t* st = base + s * C::kTmaStageBytes;
                 const int kg = k_begin + i;                         // K step in the whole of K
                 const int srow = p.gw_steps ? kg / p.gw_steps : 0;
-                mbar_arrive_expect_tx(&full_tma[s], kABytes + kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
+                mbar_arrive_expect_tx(&full_tma[s], kABytes + C::kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
                 tma_load_2d(st, &maps.a, kg * kBK, m0, &full_tma[s]);
-                tma_load_2d(st + kABytes, &maps.w, n0, kg * (kBK / 8), &full_tma[s]);
-                tma_load_2d(st + kABytes + kWBytes, &maps.s, n0, srow, &full_tma[s]);
+                tma_load_2d(st + kABytes, &maps.w, n0, kg * C::kWordRows, &full_tma[s]);
+                tma_load_2d(st + kABytes + C::kWBytes, &maps.s, n0, srow, &full_tma[s]);
                 if constexpr (HAS_ZP)
-                    tma_load_2d(st + kABytes + kWBytes + kSBytes, &maps.z, n0, srow, &full_tma[s]);
+                    tma_load_2d(st + kABytes + C::kWBytes + kSBytes, &maps.z, n0, srow, &full_tma[s]);
             }
         }
     } else if (warp == 1) {
@@ -224,14 +245,14 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
             // stage's TMA copy, so full_b alone certifies both operands.
             bool ready = mbar_try_wait(&full_b[0], 0);
             for (int i = 0; i < nsteps; ++i) {
-                const int s = i % kTmaStages, b = i % kBStages;
+                const int s = i % C::kTmaStages, b = i % kBStages;
                 if (!ready && !wait_or_abort(&full_b[b], (uint32_t)((i / kBStages) & 1), abort_flag)) break;
                 // peek at the next stage while this one's MMAs queue (no tcgen05 fence
                 // per stage: the barrier orders the operands, and a fence here would
                 // hold the issuer until the queued MMAs drain)
                 ready = (i + 1 < nsteps) &&
                         mbar_try_wait(&full_b[(i + 1) % kBStages], (uint32_t)(((i + 1) / kBStages) & 1));
-                const uint32_t a_addr = smem_addr(base + s * kTmaStageBytes);
+                const uint32_t a_addr = smem_addr(base + s * C::kTmaStageBytes);
                 const uint32_t b_addr = smem_addr(bring + b * kBBytes);
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk)
@@ -245,14 +266,14 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     } else {
         // ---------------- dequant warpgroups (warps 2..17), then epilogue
         const int n = (threadIdx.x - 64) & (kBN - 1);       // column of the tile
-        const int j0 = ((threadIdx.x - 64) >> 8) * 4;       // word rows j0 .. j0 + 3 of the K step
+        const int j0 = ((threadIdx.x - 64) >> 8) * 4;       // 16-byte units j0 .. j0 + 3 of the K step's B row
         for (int i = 0; i < nsteps; ++i) {
-            const int s = i % kTmaStages, b = i % kBStages;
-            if (!wait_or_abort(&full_tma[s], (uint32_t)((i / kTmaStages) & 1), abort_flag)) break;
+            const int s = i % C::kTmaStages, b = i % kBStages;
+            if (!wait_or_abort(&full_tma[s], (uint32_t)((i / C::kTmaStages) & 1), abort_flag)) break;
             if (i >= kBStages && !wait_or_abort(&empty_b[b], (uint32_t)(((i / kBStages) & 1) ^ 1), abort_flag)) break;
-            const uint8_t* st = base + s * kTmaStageBytes;
+            const uint8_t* st = base + s * C::kTmaStageBytes;
             const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + kABytes);
-            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kABytes + kWBytes);
+            const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kABytes + C::kWBytes);
             uint8_t* bt = bring + b * kBBytes;
             const uint16_t sbits = sp[n];
             const uint32_t s2 = h2_dup(sbits);
@@ -263,7 +284,19 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
             }
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
-                const int j = j0 + jj;
+                const int j = j0 + jj;       // 16-byte unit = 8 K values: one int4 word or two fp8 words
+                if constexpr (FP8) {
+                    // E4M3 -> fp16 is exact (subnormals included, NaN stays NaN);
+                    // fp16(w * s) is then the contract rounding of the product
+                    const uint32_t w0 = wp[(2 * j) * kBN + n], w1 = wp[(2 * j + 1) * kBN + n];
+                    uint4 o;
+                    o.x = h2_mul(e4m3x2_to_h2((uint16_t)(w0 & 0xFFFFu)), s2);
+                    o.y = h2_mul(e4m3x2_to_h2((uint16_t)(w0 >> 16)), s2);
+                    o.z = h2_mul(e4m3x2_to_h2((uint16_t)(w1 & 0xFFFFu)), s2);
+                    o.w = h2_mul(e4m3x2_to_h2((uint16_t)(w1 >> 16)), s2);
+                    *reinterpret_cast<uint4*>(bt + n * 128 + ((j ^ (n & 7)) << 4)) = o;
+                    continue;
+                }
                 const uint32_t w = wp[j * kBN + n];
                 uint32_t q[4];
                 unpack_natural<SIGNED>(w, q);
@@ -304,12 +337,17 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
             if (ok) {
                 for (int c0 = 64 * cq; c0 < 64 * cq + 64; c0 += 32) {
                     uint32_t v[32];
+                    // warp-collective: every lane loads, whatever its row
                     tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+                    // rows past M (a decode batch fills one row of 128) are
+                    // neither stored nor summed
+                    if (m0 + r < p.M) {
 #pragma unroll
-                    for (int k = 0; k < 32; k += 4)
-                        __stcg(reinterpret_cast<float4*>(mine + c0 + k),
-                               make_float4(__uint_as_float(v[k]), __uint_as_float(v[k + 1]),
-                                           __uint_as_float(v[k + 2]), __uint_as_float(v[k + 3])));
+                        for (int k = 0; k < 32; k += 4)
+                            __stcg(reinterpret_cast<float4*>(mine + c0 + k),
+                                   make_float4(__uint_as_float(v[k]), __uint_as_float(v[k + 1]),
+                                               __uint_as_float(v[k + 2]), __uint_as_float(v[k + 3])));
+                    }
                 }
             }
             __threadfence();
@@ -327,8 +365,9 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
                 // coalesced), four splits' loads in flight, in split order.
                 const int t = threadIdx.x - 64;                  // 0 .. 511
                 constexpr int kPer = kBM * kBN / 4;              // float4s in a partial
+                const int valid = min(kBM, p.M - m0) * (kBN / 4);   // float4s of the tile's rows < M
                 const float4* src = reinterpret_cast<const float4*>(p.part) + (size_t)tile * p.ksplit * kPer;
-                for (int i = t; i < kPer; i += 32 * kDqWarps) {
+                for (int i = t; i < valid; i += 32 * kDqWarps) {
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                     for (int z0 = 0; z0 < p.ksplit; z0 += 4) {
                         float4 f[4];
@@ -382,7 +421,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         // the issuer committed acc_full after its last MMA; wait for it (bounded)
         mbar_wait_bounded(acc_full, 0, kWaitLimitNs / 4);
         // and for copies still landing in the ring
-        for (int s = 0; s < kTmaStages; ++s) mbar_wait_bounded(&full_tma[s], 0, kWaitLimitNs / 8);
+        for (int s = 0; s < C::kTmaStages; ++s) mbar_wait_bounded(&full_tma[s], 0, kWaitLimitNs / 8);
     }
     __syncthreads();
     if (warp == 1) {
@@ -772,10 +811,11 @@ int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
 
 }  // namespace pair
 
-template <bool SIGNED, bool HAS_ZP>
+template <bool SIGNED, bool HAS_ZP, bool FP8 = false>
 int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
-    auto kern = gemm_w4_tc_kernel<SIGNED, HAS_ZP>;
-    const size_t smem = 1024 + (size_t)kRingBytes + kBarriers * 8 + 16;
+    using C = TcCfg<FP8>;
+    auto kern = gemm_w4_tc_kernel<SIGNED, HAS_ZP, FP8>;
+    const size_t smem = 1024 + (size_t)C::kRingBytes + C::kBarriers * 8 + 16;
     static SmemLimit limit;     // per instantiation, per device
     const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
     if (st != T4B_OK) return st;
@@ -863,4 +903,54 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
     return Z ? launch<false, true>(maps, p, stream) : launch<false, false>(maps, p, stream);
 }
 
+// FP8-E4M3 weights (4 per word, K row 4 kw + j in byte j of word (kw, n)),
+// fp16 activations: the single-CTA kernel with the E4M3 dequant, for every M
+// (a decode batch fills one 128-row tile).  Where the tiles leave SMs idle, K
+// is split as in the INT4 GEMM, here from 4 K steps a split: at small M the
+// dequant of B, which every split shares evenly, is the whole cost.
+int gemm_fp8_tc(const void* A, const void* W, const void* S, void* C, int M, int N, int K, int group,
+                cudaStream_t stream) {
+    using Cfg = TcCfg<true>;
+    if (M < 1 || (K % kBK) != 0 || (group % kBK) != 0 || (N % 8) != 0) return T4B_ERR_UNSUPPORTED;
+    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(S, 16) || !aligned(C, 16)) return T4B_ERR_UNSUPPORTED;
+    GemmParams p;
+    p.C = static_cast<uint16_t*>(C);
+    p.M = M; p.N = N; p.K = K;
+    p.ksteps = K / kBK;
+    p.gw_steps = (group >= K) ? 0 : group / kBK;
+    p.ksplit = 1;
+    p.ks_per = p.ksteps;
+    p.part = nullptr;
+    p.counters = nullptr;
+    const int sms = sm_count();
+    const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    const int ks = std::min(std::min(sms / tiles, p.ksteps / 4), 8);
+    if (ks >= 2) {
+        p.ks_per = (p.ksteps + ks - 1) / ks;
+        p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;      // no empty split
+        Workspace ws;
+        const int st = acquire_workspace(stream, (size_t)tiles, (size_t)tiles * p.ksplit * kBM * kBN, &ws);
+        if (st != T4B_OK) return st;
+        p.part = ws.part;
+        p.counters = ws.counters;
+    }
+    GemmMaps maps;
+    if (!make_tmap_2d_ex(&maps.a, true, A, (uint64_t)M, (uint64_t)K, kBM, kBK, 128, 256) ||
+        !make_tmap_2d_ex(&maps.w, false, W, (uint64_t)(K / 4), (uint64_t)N, Cfg::kWordRows, kBN, 0, 256) ||
+        !make_tmap_2d_ex(&maps.s, true, S, (uint64_t)(K / group), (uint64_t)N, 1, kBN, 0, 0))
+        return T4B_ERR_UNSUPPORTED;
+    maps.z = maps.s;
+    return launch<true, false, true>(maps, p, stream);
+}
+
 }  // namespace t4b
+
+extern "C" int t4b_fused_w8a16_gemm_fp8(const void* A, const void* W_packed, const void* scales, void* C, int M,
+                                        int N, int K, int group_size, void* stream) {
+    using namespace t4b;
+    if (M < 1 || N < 1 || K < 4 || (K % 4) != 0) return T4B_ERR_INVALID_VALUE;
+    if (group_size < 4 || (K % group_size) != 0) return T4B_ERR_INVALID_VALUE;
+    if (!A || !W_packed || !scales || !C) return T4B_ERR_NULL_POINTER;
+    if (!aligned(A, 16) || !aligned(W_packed, 16) || !aligned(scales, 16) || !aligned(C, 16)) return T4B_ERR_MISALIGNED;
+    return gemm_fp8_tc(A, W_packed, scales, C, M, N, K, group_size, static_cast<cudaStream_t>(stream));
+}

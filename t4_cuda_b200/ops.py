@@ -24,7 +24,7 @@ from . import _lib
 
 __all__ = [
     "dequantize_u4", "dequantize_s4", "dequantize_s3", "dequantize_fp8",
-    "fused_w4a16_gemm_u4", "fused_w4a16_gemm_s4", "fused_h17_gemv_s3",
+    "fused_w4a16_gemm_u4", "fused_w4a16_gemm_s4", "fused_h17_gemv_s3", "fused_w8a16_gemm_fp8",
     "set_gemv_kernel", "device_error",
 ]
 
@@ -285,6 +285,67 @@ def fused_w4a16_gemm_u4(A, W_packed, scales, zero_points):
 def fused_w4a16_gemm_s4(A, W_packed, scales, zero_points):
     """C = A @ dequant_s4(W_packed).  Mirrors bindings.cpp:99-132."""
     return _fused("t4b_fused_w4a16_gemm_s4", A, W_packed, scales, zero_points)
+
+
+# ------------------------------------------------------- FP8-E4M3 weight GEMM
+def fused_w8a16_gemm_fp8(A, W_packed, scales):
+    """C = A @ (E4M3(W_packed) * scales), fp16 in, fp32 accumulate, fp16 out.
+
+    No counterpart op in the reference (it has only the flat dequantize_fp8,
+    lop3_dequant.h:93-123): this is the fused path for its E4M3 weight format.
+    W_packed int32 [K/4, N]: byte j of word (kw, n) is the E4M3 code of K row
+    4 kw + j (the byte order of dequantize_fp8).  scales fp16 (N,), (1, N) or
+    (K/g, N).  The weight is fp16(e4m3 * s) with exact E4M3 decoding (subnormal
+    codes are values; 0x7F / 0xFF are NaN and propagate) -- unlike the
+    reference's CPU dequant, which flushes subnormal codes to 0 and reads the
+    NaN codes as 480 (tests/test_dequant_correctness.py:63-84).  The tcgen05
+    kernel takes K % 64 == 0, group % 64 == 0 and N % 8 == 0."""
+    if not (A.is_cuda and W_packed.is_cuda and scales.is_cuda):
+        _fail("A, W_packed and scales must be CUDA tensors")
+    if A.dtype != torch.float16:
+        _fail("A must be FP16")
+    if W_packed.dtype != torch.int32:
+        _fail("W_packed must be Int32")
+    if scales.dtype != torch.float16:
+        _fail("scales must be FP16")
+    if A.dim() != 2 or W_packed.dim() != 2:
+        _fail("A must be (M, K) and W_packed (K/4, N)")
+    dev = A.device
+    if W_packed.device != dev or scales.device != dev:
+        _fail("all tensors must be on the same device")
+    M, K = A.shape
+    N = W_packed.size(1)
+    if M <= 0 or N <= 0 or K <= 0:
+        _fail("Dimensions M, N, K must be positive")
+    if K % 4:
+        _fail("K must be a multiple of 4 (4 E4M3 values per int32 word)")
+    if W_packed.size(0) != K // 4:
+        _fail(f"W_packed must have K/4={K // 4} rows, got {W_packed.size(0)}")
+    if scales.dim() == 1:
+        G = 1
+        if scales.numel() != N:
+            _fail(f"scales of shape (N,) must have N={N} elements, got {scales.numel()}")
+    else:
+        if scales.dim() != 2 or scales.size(1) != N or scales.size(0) < 1 or K % scales.size(0):
+            _fail("scales must be (N,), (1, N) or (K/group, N)")
+        G = scales.size(0)
+    A_ = _aligned16(A)
+    W_ = W_packed if W_packed.is_contiguous() else W_packed.contiguous()
+    S_ = scales if scales.is_contiguous() else scales.contiguous()
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    cur = torch.cuda.current_device()
+    idx = dev.index if dev.index is not None else cur
+    if cur != idx:
+        torch.cuda.set_device(idx)
+    try:
+        st = _entry("t4b_fused_w8a16_gemm_fp8")(A_.data_ptr(), W_.data_ptr(), S_.data_ptr(), C.data_ptr(), M, N, K,
+                                                K // G, torch._C._cuda_getCurrentRawStream(idx))
+    finally:
+        if cur != idx:
+            torch.cuda.set_device(cur)
+    if st:
+        _lib.check(st, "fused_w8a16_gemm_fp8")
+    return C
 
 
 # --------------------------------------------------------------- H17 INT3 GEMV

@@ -148,3 +148,19 @@ def test_int4_packer_roundtrip():
     # the word layout of tests/test_fused_gemm_correctness.py:11-15 (row 8kw+j = nibble j)
     wu = oracle.as_u32(w)
     assert ((wu[2, 5] >> 12) & 0xF) == (q[8 * 2 + 3, 5] & 0xF)
+
+
+def test_fp8_oracle_matches_torch_e4m3fn():
+    """The FP8 GEMM oracle decodes all 256 E4M3 codes as torch.float8_e4m3fn
+    does (subnormals, NaN), and packs / unpacks bytes in K order."""
+    import torch
+    codes = np.arange(256, dtype=np.uint8)
+    mine = oracle.e4m3_to_float(codes)
+    ref = torch.from_numpy(codes).view(torch.float8_e4m3fn).double().numpy()
+    assert np.array_equal(np.isnan(mine), np.isnan(ref))
+    assert np.array_equal(mine[~np.isnan(mine)], ref[~np.isnan(ref)])
+    rng = np.random.default_rng(0)
+    c = rng.integers(0, 256, size=(64, 9), dtype=np.int64).astype(np.uint8)
+    assert np.array_equal(oracle.unpack_fp8_codes(oracle.pack_fp8(c)), c)
+    w = oracle.pack_fp8(c)
+    assert (w.view(np.uint32)[3, 2] & 0xFF) == c[12, 2] and (w.view(np.uint32)[3, 2] >> 24) == c[15, 2]

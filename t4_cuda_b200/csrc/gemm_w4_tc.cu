@@ -852,13 +852,18 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
     // M > 128: CTA pairs (each CTA dequantizes 128 of a pair's 256 columns).
     // When the tiles (or pairs) leave SMs idle and K is long, K is split
     // across CTAs (or pairs) until about one CTA per SM (at least 8 K steps a
-    // split).  Measured: gains at K >= 8192, but losses at K = 4096, where
-    // storing and re-reading the fp32 partials costs more than the idle SMs.
+    // split).  Measured: gains at K >= 8192, but losses at K = 4096 with a
+    // third or more of the SMs busy, where storing and re-reading the fp32
+    // partials costs more than the idle SMs.
     bool use_pair = M > kBM && allow_pairs;
     const int sms = sm_count();
     const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     const int pair_ctas = 2 * ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
-    if (p.ksteps >= kMinSplitK / kBK && tiles < sms && (!use_pair || pair_ctas < sms)) {
+    // Below K = 8192 only a grid of at most a quarter of the SMs splits (e.g.
+    // 4096 x 1024 at M = 512: 16 tiles; measured 165 against 139 TFLOP/s),
+    // where the idle SMs outweigh the partials' store and re-read.
+    const bool long_k = p.ksteps >= kMinSplitK / kBK;
+    if ((long_k || 4 * tiles <= sms) && tiles < sms && (!use_pair || pair_ctas < sms)) {
         auto split_of = [&](int ctas) { return std::min(std::min(sms / ctas, p.ksteps / kMinSplitSteps), 8); };
         // M > 128 splits the CTA pairs (half a single CTA's dequant per SM)
         // when each split keeps a long K run; with short runs the pair's

@@ -246,7 +246,8 @@ def int3_and_dequant(dev):
     launch in a graph, inputs rotating through >= 4x L2:
       * H17 INT3 GEMV, M = 1, K in {4100, 14340} (4096 / 14336 padded to a
         multiple of 10), N in {4096, 14336}, group 128, no zero points; bytes
-        = (K/10) N 4 + ceil(K/128) N 2 + 2 K + 2 N;
+        = (K/10) N 4 + ceil(K/128) N 2 + 2 K + 2 N; and the same shapes at
+        M = 512 and 4096 (the tcgen05 INT3 GEMM, TFLOP/s);
       * flat dequantization (s4 and s3 magic, fp8) of a 4096 x 14336 weight's
         words with per-word scales / zero points; bytes = read + written."""
     from t4_cuda_b200 import ops
@@ -265,6 +266,21 @@ def int3_and_dequant(dev):
         alg = wbytes + G * N * 2 + K * 2 + N * 2
         out["int3_gemv"][f"{K}x{N}"] = {"us": round(us, 3), "GB/s": round(alg / us / 1e3, 1)}
         del Ws
+    # INT3 prefill (M > 16: the tcgen05 INT3 GEMM), TFLOP/s = 2 M K N / time,
+    # a CUDA graph of 5 launches on one weight set (compute-bound)
+    out["int3_gemm"] = {}
+    for K, N in ((4100, 4096), (4100, 14336), (14340, 4096), (14340, 14336)):
+        G = -(-K // 128)
+        W = torch.randint(0, 2 ** 30, (K // 10, N), dtype=torch.int32, device=dev, generator=gen)
+        S = (torch.randn((G, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+        Z = torch.empty(0, dtype=torch.float16, device=dev)
+        row = {}
+        for M in (512, 4096):
+            A = torch.randn((M, K), device=dev, generator=gen).half()
+            us = _graph_us(dev, [lambda: ops.fused_h17_gemv_s3(A, W, S, Z, group_size=128)] * 5, reps=4)
+            row[f"M={M}"] = {"us": round(us, 2), "TFLOP/s": round(2.0 * M * K * N / us / 1e6, 1)}
+        out["int3_gemm"][f"{K}x{N}"] = row
+        del W
     words = 4096 // 8 * 14336
     for kind, per_word, fn in (("s4", 8, ops.dequantize_s4), ("s3", 10, ops.dequantize_s3), ("fp8", 4, None)):
         pool = max(4, (4 * l2) // (words * (4 + 4 + 2 * per_word)) + 1)

@@ -54,8 +54,8 @@ int t4b_last_cuda_error(void);
 int t4b_version(void);
 
 /* Reads (and, if `clear`, resets) the library's device error words on the
- * current device -- the decode GEMV's, the prefill GEMM's and the INT3 GEMV's
- * (one each per device), the allocation-free GEMV's (in its fixed scratch
+ * current device -- the decode GEMV's, the prefill GEMMs' (INT4 / FP8 and INT3)
+ * and the INT3 GEMV's (one each per device), the allocation-free GEMV's (in its fixed scratch
  * array) and the one
  * in the workspace kept for `stream` (if any), ORed: bit 0 = a kernel gave up
  * a bounded wait (its output is then invalid).  Synchronizes `stream`; do not
@@ -85,9 +85,11 @@ int t4b_set_gemv_kernel(int which);
 
 /* Kernel choice for the INT3 GEMV: 0 = the register-streaming kernel (the
  * default); 1 = the warp-specialized TMA-ring kernel where it applies
- * (N % 4 == 0, W 16-byte and scales 8-byte aligned), else register streaming.
- * Returns the previous choice (-1: bad argument).  No counterpart in the
- * reference. */
+ * (N % 4 == 0, W 16-byte and scales 8-byte aligned), else register streaming;
+ * 2 = register streaming at every M.  Under 0 and 1, M > 16 runs on the
+ * tcgen05 INT3 GEMM where it takes the shape (an even group_size >= 64,
+ * N % 8 == 0, 16-byte aligned operands).  Returns the previous choice (-1:
+ * bad argument).  No counterpart in the reference. */
 int t4b_set_int3_kernel(int which);
 
 /* ---- flat dequantization ----------------------------------------------

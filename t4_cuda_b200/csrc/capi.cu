@@ -338,6 +338,11 @@ int t4b_device_error(void* stream, unsigned* out, int clear) {
     st = t4b::int3_device_error(s, &int3w, clear != 0);
     if (st != T4B_OK) return st;
     *out |= int3w;
+    // the INT3 prefill GEMM
+    unsigned int3g = 0;
+    st = t4b::int3_tc_device_error(s, &int3g, clear != 0);
+    if (st != T4B_OK) return st;
+    *out |= int3g;
     // and the allocation-free GEMV, in its fixed scratch array
     unsigned fixed = 0;
     st = t4b::static_scratch_error(s, &fixed, clear != 0);

@@ -28,6 +28,7 @@
 // Every wait on an mbarrier is bounded; a timeout sets this file's device
 // error word, stops the pipeline and still frees TMEM before the CTA exits.
 #include "common.cuh"
+#include "tcgen05.cuh"
 #include "tma.cuh"
 #include "workspace.h"
 
@@ -76,51 +77,11 @@ struct GemmMaps {
     CUtensorMap z;      // zero points, same (unused without them)
 };
 
-// ---- tcgen05 wrappers (PTX ISA 8.7, sm_100a)
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-    // K-major, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes
-    // apart (stride byte offset), leading byte offset unused (1), version 1.
-    uint64_t d = (uint64_t)((addr >> 4) & 0x3FFF);
-    d |= (uint64_t)1 << 16;                 // leading byte offset (16 B units)
-    d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset
-    d |= (uint64_t)1 << 46;                 // descriptor version
-    d |= (uint64_t)2 << 61;                 // layout: 128-byte swizzle
-    return d;
-}
-
-// kind::f16 instruction descriptor: fp16 A and B (K-major), fp32 accumulator.
-constexpr uint32_t kInstrDesc = (1u << 4)                       // D format fp32
-                              | ((uint32_t)(kBN >> 3) << 17)    // N
-                              | ((uint32_t)(kBM >> 4) << 24);   // M
+// ---- tcgen05 (the shared helpers are in tcgen05.cuh)
+constexpr uint32_t kInstrDesc = tc_idesc_f16(kBM, kBN);
 
 __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        :
-        : "r"(tmem_d), "l"(da), "l"(db), "r"(kInstrDesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(addr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    tc_mma_f16(tmem_d, da, db, kInstrDesc, accumulate);
 }
 
 // Bounded wait; on timeout records the error and raises the CTA's abort flag.
@@ -479,32 +440,7 @@ static_assert(kStageBytes % 1024 == 0 && kStageBytes >= kABytes + kWBytes + 2 * 
 static_assert((kTmaStages * kStageBytes) % 1024 == 0 && kBBytes % 1024 == 0, "B slots 1024-aligned");
 
 // kind::f16, fp16 A/B K-major, fp32 accumulator, M = 256 (pair), N = 256.
-constexpr uint32_t kInstrDesc = (1u << 4) | ((uint32_t)(kCols >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Address of this CTA's shared variable `p` in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
-    return r;
-}
-
-// Arrive on a barrier of either CTA of the pair (default .release.cta
-// semantics: the shared-memory writes it publishes are this CTA's own, made
-// visible to the tensor core's async proxy by fence.proxy.async beforehand; a
-// cluster-scope release here costs a memory barrier of ~900 cycles per stage).
-__device__ __forceinline__ void arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
+constexpr uint32_t kInstrDesc = tc_idesc_f16(2 * kRows, kCols);
 
 // Bounded wait; the fast path is a single try_wait.
 __device__ __forceinline__ bool wait_pair(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -522,18 +458,7 @@ __device__ __forceinline__ bool wait_pair(uint64_t* bar, uint32_t parity, volati
 }
 
 __device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        :
-        : "r"(tmem_d), "l"(da), "l"(db), "r"(kInstrDesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void commit_pair(uint32_t cluster_addr) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
-                 : "memory");
+    tc_mma_pair_f16(tmem_d, da, db, kInstrDesc, accumulate);
 }
 
 template <bool SIGNED, bool HAS_ZP>

@@ -43,13 +43,16 @@ def set_gemv_kernel(which="auto"):
     return {v: k for k, v in _GEMV_KERNELS.items()}[prev]
 
 
-_INT3_KERNELS = {"stream": 0, "ring": 1}
+_INT3_KERNELS = {"stream": 0, "ring": 1, "gemv": 2}
 
 
 def set_int3_kernel(which="stream"):
-    """Choose the INT3 GEMV kernel process-wide: "stream" (the register-streaming
-    kernel, the default) or "ring" (the warp-specialized TMA-ring kernel where it
-    applies, else register streaming).  Returns the previous choice."""
+    """Choose the INT3 kernel process-wide: "stream" (the register-streaming
+    GEMV, the default) or "ring" (the warp-specialized TMA-ring GEMV where it
+    applies, else register streaming) -- under both, M > 16 runs on the tcgen05
+    INT3 GEMM where it takes the shape (an even group_size >= 64, N % 8 == 0,
+    16-byte aligned operands) -- or "gemv" (register streaming at every M).
+    Returns the previous choice."""
     _check(which in _INT3_KERNELS, f"which must be one of {sorted(_INT3_KERNELS)}")
     prev = _lib.load().t4b_set_int3_kernel(_INT3_KERNELS[which])
     return {v: k for k, v in _INT3_KERNELS.items()}[prev]

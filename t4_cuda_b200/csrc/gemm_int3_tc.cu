@@ -32,9 +32,10 @@
 // 64 kg mod 10 of word 64 kg / 10 on, so the stage's 8 word rows from there
 // hold it (80 values >= 64 + 9).  A dequant thread takes one column and 32
 // consecutive K values, which start at value o = (64 kg + 32 h) mod 10 of a
-// word (even, the same for the whole warp) and span 4 words.  Each fp16 pair
-// of consecutive K values is two adjacent 3-bit fields of one word (o is
-// even and a word holds ten), put under the exponent of 1024 with the top bit
+// word (even, the same for the whole warp) and span 4 words; funnel shifts
+// re-cut them into words that start at a value boundary, so every o runs the
+// same code.  Each fp16 pair of consecutive K values is then two adjacent
+// 3-bit fields of one word (o is even), put under the exponent of 1024 with the top bit
 // of each field flipped -- 1028 + q exactly -- so q = (1028 + q) - 1028 and
 // the weight is fp16(q s), rounded once (fp16(fp32((q - z) s)) with zero
 // points).  A step lies in at most two scale groups (group >= 64); a pair
@@ -169,11 +170,12 @@ struct PairScales {
     float s[2], z[2];   // with zero points
 };
 
-// One dequant thread's 32 values of column n from value O of w[0] on, as four
-// 16-byte units j = 4h .. 4h + 3 of B row n.  Pair i takes the scales of
+// One dequant thread's 32 values of column n, as the four 16-byte units
+// j = 4h .. 4h + 3 of B row n.  nw: the values as aligned words -- pair i is
+// fields 2 (i % 5), 2 (i % 5) + 1 of nw[i / 5].  Pair i takes the scales of
 // group 1 if MIXED and i >= cb, else those of group 0.
-template <int O, bool HAS_ZP, bool MIXED>
-__device__ __forceinline__ void dequant_half(const uint32_t (&w)[4], const PairScales& ps, int cb, uint8_t* brow,
+template <bool HAS_ZP, bool MIXED>
+__device__ __forceinline__ void dequant_vals(const uint32_t (&nw)[4], const PairScales& ps, int cb, uint8_t* brow,
                                              int n, int h) {
 #pragma unroll
     for (int u4 = 0; u4 < 4; ++u4) {
@@ -181,8 +183,7 @@ __device__ __forceinline__ void dequant_half(const uint32_t (&w)[4], const PairS
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int i = 4 * u4 + e;
-            const int P = O + 2 * i;
-            const uint32_t q = h2_sub(pair_s3(w[P / 10], P % 10), H2_1028);
+            const uint32_t q = h2_sub(pair_s3(nw[i / 5], 2 * (i % 5)), H2_1028);
             const bool second = MIXED && i >= cb;
             if constexpr (HAS_ZP) {
                 const float sf = second ? ps.s[1] : ps.s[0];
@@ -198,27 +199,16 @@ __device__ __forceinline__ void dequant_half(const uint32_t (&w)[4], const PairS
     }
 }
 
-// cb >= 16: every pair in group 0; cb <= 0: every pair in group 1 (moved to
-// index 0); else the step's group boundary falls inside this thread's values.
-template <int O, bool HAS_ZP>
-__device__ __forceinline__ void dequant_any(const uint32_t (&w)[4], PairScales ps, int cb, uint8_t* brow, int n,
-                                            int h) {
-    if (cb > 0 && cb < 16) {
-        dequant_half<O, HAS_ZP, true>(w, ps, cb, brow, n, h);
-        return;
-    }
-    if (cb <= 0) {
-        ps.s2[0] = ps.s2[1];
-        ps.s[0] = ps.s[1];
-        ps.z[0] = ps.z[1];
-    }
-    dequant_half<O, HAS_ZP, false>(w, ps, cb, brow, n, h);
-}
-
 // One K step of one dequant thread: column n of a tile of COLS columns, K
-// values [k0 + 32 h, k0 + 32 h + 32).  st_w: the stage's packed words (8 rows
-// x COLS), st_s: its two scale rows (and two zero-point rows after them),
-// brow: row n of the B slot.
+// values [k0 + 32 h, k0 + 32 h + 32), which start at field o of a packed word
+// (o even) and span 4 words.  They are first re-cut into words that start at
+// a value boundary (nw[u] = fields o + 10 u .. o + 10 u + 9 of the stream,
+// funnel-shifted from two words, the unused top bits dropped), so one code
+// path serves every o.  st_w: the stage's packed words (8 rows x COLS), st_s:
+// its two scale rows (and two zero-point rows after them), brow: row n of the
+// B slot.  cb >= 16: every pair in group 0; cb <= 0: every pair in group 1
+// (moved to index 0); else the step's group boundary falls inside this
+// thread's values.
 template <int COLS, bool HAS_ZP>
 __device__ __forceinline__ void dequant_step(const uint32_t* st_w, const uint16_t* st_s, int k0, int h, int n,
                                              const FastDiv& gdiv, int group, uint8_t* brow) {
@@ -229,6 +219,13 @@ __device__ __forceinline__ void dequant_step(const uint32_t* st_w, const uint16_
     uint32_t w[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) w[u] = wp[u * COLS];
+    // (w[u + 1] : w[u] << 2) >> (3 o + 2): w[u]'s 30 value bits from field o
+    // on, then w[u + 1]'s; bits 30-31 of the result are never read
+    const uint32_t sh = 3u * (uint32_t)o;
+    uint32_t nw[4];
+#pragma unroll
+    for (int u = 0; u < 3; ++u) nw[u] = __funnelshift_r(w[u] << 2, w[u + 1], sh + 2u);
+    nw[3] = w[3] >> sh;                               // pair 15: fields o, o + 1 of w[3]
     PairScales ps = {};
     const int kb = ((int)fdiv((uint32_t)k0, gdiv) + 1) * group;   // first K of the step's second group
     const int cb = (kb - klo) >> 1;                   // this thread's pairs before it (may be < 0)
@@ -240,13 +237,16 @@ __device__ __forceinline__ void dequant_step(const uint32_t* st_w, const uint16_
         ps.z[0] = h_to_f(st_s[2 * COLS + n]);
         ps.z[1] = h_to_f(st_s[3 * COLS + n]);
     }
-    switch (o) {
-        case 0: dequant_any<0, HAS_ZP>(w, ps, cb, brow, n, h); break;
-        case 2: dequant_any<2, HAS_ZP>(w, ps, cb, brow, n, h); break;
-        case 4: dequant_any<4, HAS_ZP>(w, ps, cb, brow, n, h); break;
-        case 6: dequant_any<6, HAS_ZP>(w, ps, cb, brow, n, h); break;
-        default: dequant_any<8, HAS_ZP>(w, ps, cb, brow, n, h); break;
+    if (cb > 0 && cb < 16) {
+        dequant_vals<HAS_ZP, true>(nw, ps, cb, brow, n, h);
+        return;
     }
+    if (cb <= 0) {
+        ps.s2[0] = ps.s2[1];
+        ps.s[0] = ps.s[1];
+        ps.z[0] = ps.z[1];
+    }
+    dequant_vals<HAS_ZP, false>(nw, ps, cb, brow, n, h);
 }
 
 template <bool HAS_ZP, bool A8>

@@ -86,7 +86,8 @@ int t4b_set_gemv_kernel(int which);
 /* Kernel choice for the INT3 GEMV: 0 = the register-streaming kernel (the
  * default); 1 = the warp-specialized TMA-ring kernel where it applies
  * (N % 4 == 0, W 16-byte and scales 8-byte aligned), else register streaming;
- * 2 = register streaming at every M.  Under 0 and 1, M > 16 runs on the
+ * 2 = register streaming at every M; 3 = the tcgen05 INT3 GEMM at every M
+ * where it takes the shape (else as 0).  Under 0 and 1, M > 16 runs on the
  * tcgen05 INT3 GEMM where it takes the shape (an even group_size >= 64,
  * N % 8 == 0, 16-byte aligned operands).  Returns the previous choice (-1:
  * bad argument).  No counterpart in the reference. */

@@ -72,8 +72,9 @@ int gemm_tc_device_error(cudaStream_t stream, unsigned* out, bool clear);
 // INT3 (H17 packing) prefill GEMM on tcgen05 / TMEM (M > 16, K % 10 == 0, an
 // even group >= 64, N % 8 == 0, 16-byte aligned operands);
 // T4B_ERR_UNSUPPORTED (without launching) for shapes it does not take.
+// any_m: also M <= 16 (else T4B_ERR_UNSUPPORTED for those).
 int gemm_int3_tc(const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N, int K, int group,
-                 cudaStream_t stream);
+                 bool any_m, cudaStream_t stream);
 int int3_tc_device_error(cudaStream_t stream, unsigned* out, bool clear);
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }

@@ -172,18 +172,32 @@ struct PairScales {
 
 // One dequant thread's 32 values of column n, as the four 16-byte units
 // j = 4h .. 4h + 3 of B row n.  nw: the values as aligned words -- pair i is
-// fields 2 (i % 5), 2 (i % 5) + 1 of nw[i / 5].  Pair i takes the scales of
+// fields 2 (i % 5), 2 (i % 5) + 1 of nw[i / 5] (bits 30-31 are not read).  Pair i takes the scales of
 // group 1 if MIXED and i >= cb, else those of group 0.
 template <bool HAS_ZP, bool MIXED>
 __device__ __forceinline__ void dequant_vals(const uint32_t (&nw)[4], const PairScales& ps, int cb, uint8_t* brow,
                                              int n, int h) {
+    // exact q pairs: words 0-2 whole (unpack_s3_exact gives (e_i, e_{i+5}),
+    // five byte permutes make the consecutive pairs), pair 15 from word 3
+    uint32_t qp[16];
+#pragma unroll
+    for (int u = 0; u < 3; ++u) {
+        uint32_t p[5];
+        unpack_s3_exact(nw[u], p);
+        qp[5 * u + 0] = prmt(p[0], p[1], 0x5410u);     // (e0, e1)
+        qp[5 * u + 1] = prmt(p[2], p[3], 0x5410u);     // (e2, e3)
+        qp[5 * u + 2] = prmt(p[4], p[0], 0x7610u);     // (e4, e5)
+        qp[5 * u + 3] = prmt(p[1], p[2], 0x7632u);     // (e6, e7)
+        qp[5 * u + 4] = prmt(p[3], p[4], 0x7632u);     // (e8, e9)
+    }
+    qp[15] = h2_sub(pair_s3(nw[3], 0), H2_1028);
 #pragma unroll
     for (int u4 = 0; u4 < 4; ++u4) {
         uint32_t o4[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int i = 4 * u4 + e;
-            const uint32_t q = h2_sub(pair_s3(nw[i / 5], 2 * (i % 5)), H2_1028);
+            const uint32_t q = qp[i];
             const bool second = MIXED && i >= cb;
             if constexpr (HAS_ZP) {
                 const float sf = second ? ps.s[1] : ps.s[0];
@@ -802,8 +816,8 @@ int int3_tc_device_error(cudaStream_t stream, unsigned* out, bool clear) {
 }
 
 int gemm_int3_tc(const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N, int K, int group,
-                 cudaStream_t stream) {
-    if (M <= 16 || K < 10 || (K % 10) != 0 || group < kBK || (group & 1) != 0 || (N % 8) != 0)
+                 bool any_m, cudaStream_t stream) {
+    if (M < 1 || (M <= 16 && !any_m) || K < 10 || (K % 10) != 0 || group < kBK || (group & 1) != 0 || (N % 8) != 0)
         return T4B_ERR_UNSUPPORTED;
     if (!aligned(A, 16) || !aligned(W, 16) || !aligned(S, 16) || (Z && !aligned(Z, 16)) || !aligned(C, 16))
         return T4B_ERR_UNSUPPORTED;
@@ -826,7 +840,21 @@ int gemm_int3_tc(const void* A, const void* W, const void* S, const void* Z, voi
     const int sms = sm_count();
     const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     const int pair_ctas = 2 * ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
-    if ((K >= kMinSplitK || 4 * tiles <= sms) && tiles < sms && (!use_pair || pair_ctas < sms)) {
+    if (M <= 16) {
+        // a decode batch fills one 128-row tile: the dequant of B, which every
+        // split shares evenly, is the whole cost, so K splits from 4 K steps a
+        // split up to about one CTA per SM (as the FP8 GEMM does)
+        const int ks = std::min(std::min(sms / tiles, p.ksteps / 4), 8);
+        if (ks >= 2) {
+            p.ks_per = (p.ksteps + ks - 1) / ks;
+            p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;
+            Workspace ws;
+            const int st = acquire_workspace(stream, (size_t)tiles, (size_t)tiles * p.ksplit * kBM * kBN, &ws);
+            if (st != T4B_OK) return st;
+            p.part = ws.part;
+            p.counters = ws.counters;
+        }
+    } else if ((K >= kMinSplitK || 4 * tiles <= sms) && tiles < sms && (!use_pair || pair_ctas < sms)) {
         auto split_of = [&](int ctas) { return std::min(std::min(sms / ctas, p.ksteps / kMinSplitSteps), 8); };
         if (use_pair) {
             const int kp = split_of(pair_ctas);

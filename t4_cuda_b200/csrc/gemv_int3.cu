@@ -29,7 +29,8 @@ constexpr int kWarps = 8;
 
 // 0: register streaming (the default); 1: the warp-specialized TMA-ring form
 // where it applies; 2: register streaming at every M (0 and 1 run M > 16 on
-// the tcgen05 GEMM where it takes the shape).  The ring form is correct and tested but slower on every
+// the tcgen05 GEMM where it takes the shape); 3: the tcgen05 GEMM at every M
+// where it takes the shape.  The ring form is correct and tested but slower on every
 // benchmarked shape (14340 x 14336: 99 against 63 us): the step math -- ~9
 // integer and ~10 fp16 operations per 10-weight word for the exact contract
 // dequant with per-element group selection -- bounds this kernel, not the
@@ -697,8 +698,8 @@ int fused_int3(const void* A, const void* W, const void* S, const void* Z, void*
     cudaStream_t s = static_cast<cudaStream_t>(stream_);
     const int choice = g_int3_kernel.load();
     // M > 16: the tcgen05 GEMM where it takes the shape
-    if (M > 16 && choice != 2) {
-        const int st = gemm_int3_tc(A, W, S, Z, C, M, N, K, group, s);
+    if ((M > 16 && choice != 2) || choice == 3) {
+        const int st = gemm_int3_tc(A, W, S, Z, C, M, N, K, group, choice == 3, s);
         if (st != T4B_ERR_UNSUPPORTED) return st;
     }
     if (choice == 1) {
@@ -736,7 +737,7 @@ int int3_device_error(cudaStream_t stream, unsigned* out, bool clear) {
 }  // namespace t4b
 
 extern "C" int t4b_set_int3_kernel(int which) {
-    if (which < 0 || which > 2) return -1;
+    if (which < 0 || which > 3) return -1;
     return t4b::g_int3_kernel.exchange(which);
 }
 

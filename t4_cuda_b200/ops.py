@@ -43,7 +43,7 @@ def set_gemv_kernel(which="auto"):
     return {v: k for k, v in _GEMV_KERNELS.items()}[prev]
 
 
-_INT3_KERNELS = {"stream": 0, "ring": 1, "gemv": 2}
+_INT3_KERNELS = {"stream": 0, "ring": 1, "gemv": 2, "tc": 3}
 
 
 def set_int3_kernel(which="stream"):
@@ -51,8 +51,9 @@ def set_int3_kernel(which="stream"):
     GEMV, the default) or "ring" (the warp-specialized TMA-ring GEMV where it
     applies, else register streaming) -- under both, M > 16 runs on the tcgen05
     INT3 GEMM where it takes the shape (an even group_size >= 64, N % 8 == 0,
-    16-byte aligned operands) -- or "gemv" (register streaming at every M).
-    Returns the previous choice."""
+    16-byte aligned operands) -- or "gemv" (register streaming at every M), or
+    "tc" (the tcgen05 GEMM at every M where it takes the shape).  Returns the
+    previous choice."""
     _check(which in _INT3_KERNELS, f"which must be one of {sorted(_INT3_KERNELS)}")
     prev = _lib.load().t4b_set_int3_kernel(_INT3_KERNELS[which])
     return {v: k for k, v in _INT3_KERNELS.items()}[prev]

@@ -1,0 +1,145 @@
+// Torch binding of the fused matmul ops -- the role of src/bindings.cpp:64-250
+// in the reference (a torch C++ extension), in front of this library's C ABI.
+//
+// The decode path calls a fused op once per projection per token, so the
+// per-call host cost bounds a step run from Python: this binding does the
+// argument checks, the output allocation and the launch in C++ (the same
+// checks, in the same order and with the same messages, as the Python path in
+// ops.py, which mirrors bindings.cpp).  It calls the C ABI through function
+// pointers taken from the library that ops.py has loaded (init), so the
+// process has one copy of the library's state (kernel choices, caches).
+#include <torch/extension.h>
+
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace {
+
+// t4b_fused_w4a16_gemm_{u4,s4}(A, W, S, Z, C, M, N, K, group, stream)
+using FusedFn = int (*)(const void*, const void*, const void*, const void*, void*, int, int, int, int, void*);
+using StatusStringFn = const char* (*)(int);
+using LastCudaErrorFn = int (*)();
+
+FusedFn g_u4 = nullptr, g_s4 = nullptr;
+StatusStringFn g_status_string = nullptr;
+LastCudaErrorFn g_last_cuda_error = nullptr;
+PyObject* g_error_class = nullptr;      // t4_cuda_b200._lib.T4BError (a RuntimeError)
+
+[[noreturn]] void fail(const std::string& msg) { throw std::runtime_error(msg); }
+
+// A non-zero status as the library's error class, with the message of _lib.check.
+[[noreturn]] void raise_status(int st, const char* op) {
+    std::string msg = std::string(op) + ": " + (g_status_string ? g_status_string(st) : "error") + " (status " +
+                      std::to_string(st);
+    const int cuda = (st == 5 && g_last_cuda_error) ? g_last_cuda_error() : 0;
+    if (cuda) msg += ", cudaError " + std::to_string(cuda);
+    msg += ")";
+    PyErr_SetString(g_error_class ? g_error_class : PyExc_RuntimeError, msg.c_str());
+    throw pybind11::error_already_set();
+}
+
+// (N,) / (1, N) / (G, N) -> number of rows G, with the checks of ops._group_rows.
+int64_t group_rows(const torch::Tensor& t, int64_t N, int64_t K, const char* what, int64_t word_values) {
+    const int64_t d = t.dim();
+    if (d == 1) {
+        if (t.numel() != N)
+            fail(std::string(what) + " of shape (N,) must have N=" + std::to_string(N) + " elements, got " +
+                 std::to_string(t.numel()));
+        return 1;
+    }
+    if (d != 2) fail(std::string(what) + " must be 1-D (N,) or 2-D (K/group, N)");
+    if (t.size(1) != N)
+        fail(std::string(what) + " must have N=" + std::to_string(N) + " columns, got " + std::to_string(t.size(1)));
+    const int64_t G = t.size(0);
+    if (G < 1 || K % G)
+        fail(std::string(what) + ": " + std::to_string(G) + " groups must divide K=" + std::to_string(K));
+    if ((K / G) % word_values)
+        fail(std::string(what) + ": group size K/" + std::to_string(G) + "=" + std::to_string(K / G) +
+             " must be a multiple of " + std::to_string(word_values));
+    return G;
+}
+
+// Contiguous tensor whose data pointer is 16-byte aligned (copy if not).
+torch::Tensor aligned16(const torch::Tensor& t) {
+    torch::Tensor c = t.is_contiguous() ? t : t.contiguous();
+    if (reinterpret_cast<uintptr_t>(c.data_ptr()) % 16) c = c.clone();
+    return c;
+}
+
+bool has_values(const c10::optional<torch::Tensor>& z) { return z.has_value() && z->defined() && z->numel() > 0; }
+
+// ops._fused: C = A @ dequant_w4(W_packed), bindings.cpp:64-132.
+torch::Tensor fused_w4(FusedFn fn, const char* name, const torch::Tensor& A, const torch::Tensor& W,
+                       const torch::Tensor& S, const c10::optional<torch::Tensor>& Zopt) {
+    if (!fn) fail("t4_cuda_b200 torch binding not initialised");
+    if (!A.is_cuda()) fail("A must be a CUDA tensor");
+    if (!W.is_cuda()) fail("W_packed must be a CUDA tensor");
+    if (!S.is_cuda()) fail("scales must be a CUDA tensor");
+    const bool has_zp = has_values(Zopt);
+    if (has_zp) {
+        if (!Zopt->is_cuda()) fail("zero_points must be a CUDA tensor");
+        if (Zopt->scalar_type() != torch::kFloat16) fail("zero_points must be FP16");
+    }
+    if (A.scalar_type() != torch::kFloat16) fail("A must be FP16");
+    if (W.scalar_type() != torch::kInt32) fail("W_packed must be Int32");
+    if (S.scalar_type() != torch::kFloat16) fail("scales must be FP16");
+    if (A.dim() != 2) fail("A must be a 2-D (M, K) tensor");
+    if (W.dim() != 2) fail("W_packed must be a 2-D (K/8, N) tensor");
+    const auto dev = A.device();
+    if (W.device() != dev || S.device() != dev || (has_zp && Zopt->device() != dev))
+        fail("all tensors must be on the same device");
+    const int64_t M = A.size(0), K = A.size(1), N = W.size(1);
+    if (M <= 0 || N <= 0 || K <= 0) fail("Dimensions M, N, K must be positive");
+    if (K % 8) fail("K must be a multiple of 8 (8 INT4 values per int32 word)");
+    if (W.size(0) != K / 8)
+        fail("W_packed must have K/8=" + std::to_string(K / 8) + " rows, got " + std::to_string(W.size(0)));
+    const int64_t G = group_rows(S, N, K, "scales", 8);
+    if (has_zp && group_rows(*Zopt, N, K, "zero_points", 8) != G) fail("zero_points must have the same shape as scales");
+    const torch::Tensor A_ = aligned16(A);
+    const torch::Tensor W_ = W.is_contiguous() ? W : W.contiguous();
+    const torch::Tensor S_ = S.is_contiguous() ? S : S.contiguous();
+    torch::Tensor Z_;
+    if (has_zp) Z_ = Zopt->is_contiguous() ? *Zopt : Zopt->contiguous();
+    const c10::cuda::CUDAGuard guard(dev);
+    torch::Tensor C = torch::empty({M, N}, A.options());
+    const int st = fn(A_.data_ptr(), W_.data_ptr(), S_.data_ptr(), has_zp ? Z_.data_ptr() : nullptr, C.data_ptr(),
+                      (int)M, (int)N, (int)K, (int)(K / G), c10::cuda::getCurrentCUDAStream(dev.index()).stream());
+    if (st) raise_status(st, name);
+    return C;
+}
+
+torch::Tensor fused_w4a16_gemm_u4(const torch::Tensor& A, const torch::Tensor& W, const torch::Tensor& S,
+                                  const c10::optional<torch::Tensor>& Z) {
+    return fused_w4(g_u4, "t4b_fused_w4a16_gemm_u4", A, W, S, Z);
+}
+
+torch::Tensor fused_w4a16_gemm_s4(const torch::Tensor& A, const torch::Tensor& W, const torch::Tensor& S,
+                                  const c10::optional<torch::Tensor>& Z) {
+    return fused_w4(g_s4, "t4b_fused_w4a16_gemm_s4", A, W, S, Z);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.doc() = "torch binding of t4_cuda_b200's fused W4A16 ops (the hot path of ops.py)";
+    m.def(
+        "init",
+        [](uintptr_t u4, uintptr_t s4, uintptr_t status_string, uintptr_t last_cuda_error, pybind11::object error_class) {
+            g_u4 = reinterpret_cast<FusedFn>(u4);
+            g_s4 = reinterpret_cast<FusedFn>(s4);
+            g_status_string = reinterpret_cast<StatusStringFn>(status_string);
+            g_last_cuda_error = reinterpret_cast<LastCudaErrorFn>(last_cuda_error);
+            Py_XDECREF(g_error_class);
+            g_error_class = error_class.ptr();
+            Py_XINCREF(g_error_class);
+        },
+        "Entry points of the loaded C library (addresses) and the error class.");
+    m.def("fused_w4a16_gemm_u4", &fused_w4a16_gemm_u4, "C = A @ dequant_u4(W_packed)", pybind11::arg("A"),
+          pybind11::arg("W_packed"), pybind11::arg("scales"), pybind11::arg("zero_points"));
+    m.def("fused_w4a16_gemm_s4", &fused_w4a16_gemm_s4, "C = A @ dequant_s4(W_packed)", pybind11::arg("A"),
+          pybind11::arg("W_packed"), pybind11::arg("scales"), pybind11::arg("zero_points"));
+}

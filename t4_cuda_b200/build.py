@@ -82,5 +82,47 @@ def build(verbose=False, force=False):
     return LIB
 
 
+BIND_SRC = os.path.join(PKG, "bind", "torch_ops.cpp")
+
+
+def binding_path():
+    """In-tree path of the torch binding module (``_torch_ops``)."""
+    import sysconfig
+    return os.path.join(PKG, "_torch_ops" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_binding(verbose=False, force=False):
+    """Compile the torch binding of the fused ops (bind/torch_ops.cpp) with the
+    host compiler against the installed torch; returns its path."""
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension
+    out = binding_path()
+    if not force and not _stale(out, [BIND_SRC]):
+        return out
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "c++"
+    abi = int(bool(torch._C._GLIBCXX_USE_CXX11_ABI))
+    inc = cpp_extension.include_paths() + [sysconfig.get_paths()["include"], os.path.join(_cuda_home(), "include")]
+    libdirs = cpp_extension.library_paths()
+    cmd = ([cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+            "-DTORCH_EXTENSION_NAME=_torch_ops", "-DTORCH_API_INCLUDE_EXTENSION_H"]
+           + ["-I" + d for d in inc] + [BIND_SRC, "-o", out + ".tmp"]
+           + ["-L" + d for d in libdirs] + ["-Wl,-rpath," + d for d in libdirs]
+           + ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python"])
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"torch binding build failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(out + ".tmp", out)
+    if verbose:
+        print(f"[t4b200] built {out}", file=sys.stderr)
+    return out
+
+
+def _cuda_home():
+    nv = nvcc()
+    return os.path.dirname(os.path.dirname(os.path.realpath(nv)))
+
+
 if __name__ == "__main__":
     build(verbose=True, force="--force" in sys.argv)
+    build_binding(verbose=True, force="--force" in sys.argv)

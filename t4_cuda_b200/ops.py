@@ -281,13 +281,43 @@ def _fused(name, A, W_packed, scales, zero_points):
     return C
 
 
+_BIND = False      # the torch binding module once looked up (None: not built)
+
+
+def _binding():
+    """The torch binding of the fused W4A16 ops (bind/torch_ops.cpp, built in-tree
+    as ``_torch_ops`` next to the library), initialised with the loaded
+    library's entry points; None if it has not been built.  It does the same
+    checks as ``_fused`` in C++, which takes the per-call host cost of a decode
+    step's ~224 calls from ~11 to a few microseconds."""
+    global _BIND
+    if _BIND is False:
+        import ctypes
+        import importlib.util
+        b = None
+        if importlib.util.find_spec(__package__ + "._torch_ops") is not None:
+            from . import _torch_ops as b   # a build that does not load is an error, not a fallback
+            lib = _lib.load()
+            addr = lambda f: ctypes.cast(f, ctypes.c_void_p).value    # noqa: E731
+            b.init(addr(lib.t4b_fused_w4a16_gemm_u4), addr(lib.t4b_fused_w4a16_gemm_s4),
+                   addr(lib.t4b_status_string), addr(lib.t4b_last_cuda_error), _lib.T4BError)
+        _BIND = b
+    return _BIND
+
+
 def fused_w4a16_gemm_u4(A, W_packed, scales, zero_points):
     """C = A @ dequant_u4(W_packed).  Mirrors bindings.cpp:64-97."""
+    b = _BIND if _BIND is not False else _binding()
+    if b is not None:
+        return b.fused_w4a16_gemm_u4(A, W_packed, scales, zero_points)
     return _fused("t4b_fused_w4a16_gemm_u4", A, W_packed, scales, zero_points)
 
 
 def fused_w4a16_gemm_s4(A, W_packed, scales, zero_points):
     """C = A @ dequant_s4(W_packed).  Mirrors bindings.cpp:99-132."""
+    b = _BIND if _BIND is not False else _binding()
+    if b is not None:
+        return b.fused_w4a16_gemm_s4(A, W_packed, scales, zero_points)
     return _fused("t4b_fused_w4a16_gemm_s4", A, W_packed, scales, zero_points)
 
 

@@ -27,6 +27,8 @@
 //               latency-bound: with fewer the tensor pipe idles waiting for B.
 // Every wait on an mbarrier is bounded; a timeout sets this file's device
 // error word, stops the pipeline and still frees TMEM before the CTA exits.
+#include <atomic>
+
 #include "common.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
@@ -62,6 +64,10 @@ struct GemmParams {
     // each CTA stores its fp32 tile to part, and the last of a tile's CTAs
     // (counter) sums the ksplit partials in split order and writes C
     int ksplit, ks_per;
+    // single-CTA kernel: 1 = the ksplit CTAs of a tile are one thread-block
+    // cluster and add their fp32 tiles through distributed shared memory; 0 =
+    // through global memory (part, counters)
+    int cluster_split;
     float* part;            // [tiles][ksplit][128][256]
     unsigned* counters;     // one per tile, zero between launches
 };
@@ -69,6 +75,7 @@ struct GemmParams {
 constexpr int kMinSplitSteps = 8;       // K steps (512 K) a split takes at least
 constexpr int kMinSplitK = 8192;        // K below which the GEMM never splits K
 constexpr int kMinPairSplitSteps = 96;  // K steps a split of a CTA pair takes at least
+constexpr int kMinLooseSplitSteps = 16; // ... when the grid fills more than a quarter of the SMs
 
 struct GemmMaps {
     CUtensorMap a;      // A [M, K] fp16, box 64 x 128, 128-byte swizzle
@@ -112,6 +119,16 @@ __device__ __forceinline__ void unpack_natural(uint32_t w, uint32_t (&q)[4]) {
     }
 }
 
+// Split K in a cluster: a CTA's fp32 tile in shared memory, rows 257 floats apart.
+constexpr int kRedPitch = kBN + 1;
+
+// A 32-bit load from shared memory of a CTA of this cluster (address from mapa).
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+
 // Per weight format of the single-CTA kernel: INT4 packs 8 K values in a word
 // (8 word rows per K step of 64), FP8-E4M3 4 (16 word rows, a twice larger
 // packed tile, so one TMA stage fewer fits in shared memory).
@@ -124,6 +141,9 @@ struct TcCfg {
     static constexpr int kRingBytes = kTmaStages * kTmaStageBytes + kBStages * kBBytes;
     static constexpr int kBarriers = 2 * kTmaStages + 2 * kBStages + 1;
 };
+
+static_assert(kBM * kRedPitch * 4 <= TcCfg<false>::kRingBytes && kBM * kRedPitch * 4 <= TcCfg<true>::kRingBytes,
+              "a CTA's fp32 tile fits in its ring");
 
 // Two E4M3 bytes (low byte first) -> fp16x2 (low half first), exactly.
 __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint16_t v) {
@@ -284,7 +304,23 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
         const int quarter = warp & 3;                       // TMEM lanes this warp may read
         const int cq = (warp - 2) >> 2;                     // which 64 columns
         const int row = m0 + 32 * quarter + lane;
-        if (p.ksplit > 1) {
+        if (p.ksplit > 1 && p.cluster_split) {
+            // Split K in a cluster: this CTA's fp32 tile goes to its own shared
+            // memory -- the ring, idle now (acc_full: every MMA has completed,
+            // so every copy has landed and been read) -- as [128][kRedPitch]
+            // (pitch 257: the 32 rows a warp writes fall in 32 distinct banks);
+            // the peers add the tiles after the cluster barrier below.
+            if (ok) {
+                float* tile = reinterpret_cast<float*>(base);
+                const int r = 32 * quarter + lane;
+                for (int c0 = 64 * cq; c0 < 64 * cq + 64; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);   // warp-collective
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) tile[r * kRedPitch + c0 + k] = __uint_as_float(v[k]);
+                }
+            }
+        } else if (p.ksplit > 1) {
             // Split K: this CTA's fp32 tile goes to its partial slot; the last
             // CTA of the tile to arrive adds the ksplit partials in split order
             // -- the same sum whichever CTA is last.  Every
@@ -373,6 +409,37 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
                 }
             }
         }
+    }
+
+    if (p.ksplit > 1 && p.cluster_split) {
+        // Every thread of every CTA of the cluster (one tile, its K splits)
+        // passes both barriers, whatever path it took above.
+        cluster_sync_all();      // every CTA's fp32 tile is in its shared memory
+        if (warp >= 2 && !*abort_flag) {
+            // CTA `rank` adds, for its share of the tile's elements (rows < M
+            // only, row-major, consecutive threads on consecutive columns), the
+            // ksplit tiles in split order -- the same sum on every run.
+            const int ks = p.ksplit;
+            const int rank = (int)cluster_rank();
+            const int rows = min(kBM, p.M - m0);
+            const int E = rows * kBN;
+            const int per = (E + ks - 1) / ks;
+            const int e_end = min(E, (rank + 1) * per);
+            const uint32_t tile0 = smem_addr(base);
+            uint32_t peer[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) peer[q] = q < ks ? map_to_rank(base, (uint32_t)q) : tile0;
+            for (int e = rank * per + (int)threadIdx.x - 64; e < e_end; e += 32 * kDqWarps) {
+                const int r = e >> 8, c = e & (kBN - 1);
+                const uint32_t off = (uint32_t)(r * kRedPitch + c) * 4u;
+                float v = 0.f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (q < ks) v += ld_dsmem_f32(peer[q] + off);
+                if (n0 + c < p.N) p.C[(size_t)(m0 + r) * p.N + n0 + c] = __half_as_ushort(__float2half_rn(v));
+            }
+        }
+        cluster_sync_all();      // no CTA leaves while a peer still reads its tile
     }
 
     // ---------------- teardown: no MMA may still be writing TMEM when it is freed
@@ -745,8 +812,73 @@ int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
     const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
     if (st != T4B_OK) return st;
     dim3 grid((p.N + kBN - 1) / kBN, (p.M + kBM - 1) / kBM, p.ksplit);
+    if (p.ksplit > 1 && p.cluster_split) {
+        // the K splits of a tile form one cluster (at most 8 CTAs)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = (unsigned)p.ksplit;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        return check_launch();
+    }
     kern<<<grid, kThreads, smem, stream>>>(maps, p);
     return check_launch();
+}
+
+// How many clusters of `ks` single-CTA GEMM CTAs can be resident at once on
+// the current device (cached per device and size): a cluster must fit in one
+// GPC, so large clusters of one-CTA-per-SM kernels can fit fewer times than
+// the SM count suggests (measured: 16 clusters of 8 ran in two waves).
+int cluster_capacity(int ks) {
+    static std::atomic<int> cached[64][9];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (ks < 2 || ks > 8) return 0;
+    if (dev >= 0 && dev < 64) {
+        const int c = cached[dev][ks].load(std::memory_order_relaxed);
+        if (c > 0) return c - 1;
+    }
+    using C = TcCfg<false>;
+    auto kern = gemm_w4_tc_kernel<true, false, false>;
+    const size_t smem = 1024 + (size_t)C::kRingBytes + C::kBarriers * 8 + 16;
+    static SmemLimit limit;
+    int n = 0;
+    if (ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit) == T4B_OK) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1, 1, (unsigned)ks);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = (unsigned)ks;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+    }
+    if (dev >= 0 && dev < 64) cached[dev][ks].store(n + 1, std::memory_order_relaxed);
+    return n;
+}
+
+// The largest split of `tiles` single-CTA tiles into clusters of at most `ks`
+// that are all resident at once (1: none).
+int cluster_split_of(int tiles, int ks) {
+    for (; ks >= 2; --ks)
+        if (tiles <= cluster_capacity(ks)) return ks;
+    return 1;
 }
 
 }  // namespace
@@ -772,6 +904,7 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
     p.gw_steps = (group >= K) ? 0 : group / kBK;
     p.ksplit = 1;
     p.ks_per = p.ksteps;
+    p.cluster_split = 0;
     p.part = nullptr;
     p.counters = nullptr;
     // M > 128: CTA pairs (each CTA dequantizes 128 of a pair's 256 columns).
@@ -784,12 +917,16 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
     const int sms = sm_count();
     const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     const int pair_ctas = 2 * ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
-    // Below K = 8192 only a grid of at most a quarter of the SMs splits (e.g.
-    // 4096 x 1024 at M = 512: 16 tiles; measured 165 against 139 TFLOP/s),
-    // where the idle SMs outweigh the partials' store and re-read.
+    // Below K = 8192 a grid of at most a quarter of the SMs splits from 8 K
+    // steps a split, one of at most half the SMs from 16 (single CTAs, whose
+    // splits add up in a cluster; measured at M = 512: 4096 x 1024 168 -> 247
+    // TFLOP/s, 4096 x 4096 541 -> 617; at 8 K steps a split of a 64-tile grid
+    // the cluster's fixed cost lost, 323 -> 279).
     const bool long_k = p.ksteps >= kMinSplitK / kBK;
-    if ((long_k || 4 * tiles <= sms) && tiles < sms && (!use_pair || pair_ctas < sms)) {
-        auto split_of = [&](int ctas) { return std::min(std::min(sms / ctas, p.ksteps / kMinSplitSteps), 8); };
+    const bool quarter = 4 * tiles <= sms;
+    if ((long_k || 2 * tiles <= sms) && tiles < sms && (!use_pair || pair_ctas < sms)) {
+        const int min_steps = (long_k || quarter) ? kMinSplitSteps : kMinLooseSplitSteps;
+        auto split_of = [&](int ctas) { return std::min(std::min(sms / ctas, p.ksteps / min_steps), 8); };
         // M > 128 splits the CTA pairs (half a single CTA's dequant per SM)
         // when each split keeps a long K run; with short runs the pair's
         // larger fixed cost wins out (measured against single CTAs: +5-10 % at
@@ -797,13 +934,19 @@ int gemm_w4_tc(bool is_signed, const void* A, const void* W, const void* S, cons
         // single CTAs split instead.  Either way a partial
         // is one CTA's 128 x 256 accumulator.
         if (use_pair) {
-            const int kp = split_of(pair_ctas);
+            const int kp = (long_k || quarter) ? split_of(pair_ctas) : 1;
             const bool pair_split = kp >= 2 && (p.ksteps + kp - 1) / kp >= kMinPairSplitSteps;
-            if (!pair_split && split_of(tiles) >= 2) use_pair = false;
+            if (!pair_split && cluster_split_of(tiles, split_of(tiles)) >= 2) use_pair = false;
         }
         const int ctas = use_pair ? pair_ctas : tiles;
-        const int ks = split_of(ctas);
-        if (ks >= 2) {
+        const int ks = use_pair ? split_of(ctas) : cluster_split_of(tiles, split_of(tiles));
+        if (ks >= 2 && !use_pair) {
+            // single CTAs: the splits of a tile are one cluster and add their
+            // tiles through distributed shared memory (no workspace)
+            p.ks_per = (p.ksteps + ks - 1) / ks;
+            p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;      // no empty split
+            p.cluster_split = 1;
+        } else if (ks >= 2) {
             p.ks_per = (p.ksteps + ks - 1) / ks;
             p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;      // no empty split
             Workspace ws;
@@ -850,19 +993,16 @@ int gemm_fp8_tc(const void* A, const void* W, const void* S, void* C, int M, int
     p.gw_steps = (group >= K) ? 0 : group / kBK;
     p.ksplit = 1;
     p.ks_per = p.ksteps;
+    p.cluster_split = 0;
     p.part = nullptr;
     p.counters = nullptr;
     const int sms = sm_count();
     const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-    const int ks = std::min(std::min(sms / tiles, p.ksteps / 4), 8);
+    const int ks = cluster_split_of(tiles, std::min(std::min(sms / tiles, p.ksteps / 4), 8));
     if (ks >= 2) {
         p.ks_per = (p.ksteps + ks - 1) / ks;
         p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;      // no empty split
-        Workspace ws;
-        const int st = acquire_workspace(stream, (size_t)tiles, (size_t)tiles * p.ksplit * kBM * kBN, &ws);
-        if (st != T4B_OK) return st;
-        p.part = ws.part;
-        p.counters = ws.counters;
+        p.cluster_split = 1;                                  // a cluster of splits per tile
     }
     GemmMaps maps;
     if (!make_tmap_2d_ex(&maps.a, true, A, (uint64_t)M, (uint64_t)K, kBM, kBK, 128, 256) ||

@@ -195,6 +195,36 @@ uint32_t tmap_hash(const TmapKey& k) {
 
 }  // namespace
 
+int max_active_clusters(const void* kernel, int smem, int threads, int ks, ClusterCapacityCache* cache) {
+    if (ks < 2 || ks > 8) return 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64) {
+        const int c = cache->n[dev][ks].load(std::memory_order_relaxed);
+        if (c > 0) return c - 1;
+    }
+    int n = 0;
+    if (ensure_dynamic_smem(kernel, smem, &cache->limit) == T4B_OK) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1, 1, (unsigned)ks);
+        cfg.blockDim = dim3((unsigned)threads, 1, 1);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = (unsigned)ks;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+    }
+    if (dev >= 0 && dev < 64) cache->n[dev][ks].store(n + 1, std::memory_order_relaxed);
+    return n;
+}
+
 bool make_tmap_2d_ex(CUtensorMap* map, bool fp16, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
                      uint32_t box_cols, int swizzle_bytes, int l2_promotion_bytes) {
     const TmapKey key{base, rows, cols, box_rows, box_cols, swizzle_bytes, l2_promotion_bytes, fp16 ? 1 : 0};

@@ -4,6 +4,8 @@
 // (".rn" forms) so the optimizer cannot contract or reorder it.
 #pragma once
 
+#include <atomic>
+
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -78,6 +80,16 @@ int gemm_int3_tc(const void* A, const void* W, const void* S, const void* Z, voi
 int int3_tc_device_error(cudaStream_t stream, unsigned* out, bool clear);
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Clusters of `ks` CTAs (1 x 1 x ks) of `kernel` (dynamic shared memory
+// `smem`, `threads` a CTA) that can be resident at once on the current device
+// (cudaOccupancyMaxActiveClusters; 0 if none or on error), cached per device
+// and size in `cache`.  ks: 2..8.
+struct ClusterCapacityCache {
+    std::atomic<int> n[64][9];
+    SmemLimit limit;            // the kernel's dynamic shared-memory attribute, per device
+};
+int max_active_clusters(const void* kernel, int smem, int threads, int ks, ClusterCapacityCache* cache);
 
 // Division by a runtime constant d >= 1 for numerators n < 2^31:
 // n / d == (umulhi(n, mul) + n) >> shift  (Granlund & Montgomery, PLDI 1994).

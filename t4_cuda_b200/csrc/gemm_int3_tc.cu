@@ -77,6 +77,9 @@ constexpr uint32_t kInstrDesc = tc_idesc_f16(kBM, kBN);
 constexpr int kMinSplitSteps = 8;       // K steps a split takes at least
 constexpr int kMinSplitK = 8192;        // K from which any under-filled grid splits K
 constexpr int kMinPairSplitSteps = 96;  // K steps a split of a CTA pair takes at least
+constexpr int kMinLooseSplitSteps = 16; // ... when the grid fills more than a quarter of the SMs
+constexpr int kRedPitch = kBN + 1;      // a CTA's fp32 tile in shared memory (cluster split), row pitch
+static_assert(kBM * kRedPitch * 4 <= kRingBytes, "a CTA's fp32 tile fits in its ring");
 static_assert(kStageBytes % 1024 == 0, "every A tile 1024-byte aligned");
 static_assert(kStages > kInFlight, "a stage is signalled before the loader needs its slot again");
 
@@ -91,6 +94,7 @@ struct Int3TcParams {
     FastDiv gdiv;           // division by group
     int ksteps;             // ceil(K / 64)
     int ksplit, ks_per;     // split K as in the INT4 GEMM
+    int cluster_split;      // single-CTA kernel: the splits of a tile are one cluster (else part / counters)
     float* part;            // [tiles][ksplit][128][256]
     unsigned* counters;     // one per tile, zero between launches
 };
@@ -392,7 +396,20 @@ gemm_int3_tc_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcParams 
         const int quarter = warp & 3;                       // TMEM lanes this warp may read
         const int cq = (warp - kDq0) >> 2;                  // which 64 columns
         const int r = 32 * quarter + lane;
-        if (p.ksplit > 1) {
+        if (p.ksplit > 1 && p.cluster_split) {
+            // Split K in a cluster: the fp32 tile goes to this CTA's ring (idle
+            // once acc_full has fired), rows kRedPitch floats apart; the peers
+            // add the tiles after the cluster barrier below.
+            if (ok) {
+                float* tile = reinterpret_cast<float*>(base);
+                for (int c0 = 64 * cq; c0 < 64 * cq + 64; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);   // warp-collective
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) tile[r * kRedPitch + c0 + k] = __uint_as_float(v[k]);
+                }
+            }
+        } else if (p.ksplit > 1) {
             // Split K: the fp32 tile goes to this CTA's partial slot; the last
             // CTA of the tile to arrive sums the partials in split order (the
             // same sum whichever CTA is last).  Every thread reaches both
@@ -473,6 +490,35 @@ gemm_int3_tc_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcParams 
                 }
             }
         }
+    }
+
+    if (p.ksplit > 1 && p.cluster_split) {
+        // Every thread of every CTA of the cluster (one tile, its K splits)
+        // passes both barriers, whatever path it took above.
+        cluster_sync_all();      // every CTA's fp32 tile is in its shared memory
+        if (warp >= kDq0 && !*abort_flag) {
+            // CTA `rank` adds its share of the tile's elements (rows < M) over
+            // the splits in split order and stores C
+            const int ks = p.ksplit;
+            const int rank = (int)cluster_rank();
+            const int rows = min(kBM, p.M - m0);
+            const int E = rows * kBN;
+            const int per = (E + ks - 1) / ks;
+            const int e_end = min(E, (rank + 1) * per);
+            uint32_t peer[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) peer[q] = map_to_rank(base, (uint32_t)(q < ks ? q : 0));
+            for (int e = rank * per + (int)threadIdx.x - 32 * kDq0; e < e_end; e += 32 * kDqWarps) {
+                const int rr = e >> 8, c = e & (kBN - 1);
+                const uint32_t off = (uint32_t)(rr * kRedPitch + c) * 4u;
+                float v = 0.f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (q < ks) v += ld_dsmem_f32(peer[q] + off);
+                if (n0 + c < p.N) p.C[(size_t)(m0 + rr) * p.N + n0 + c] = __half_as_ushort(__float2half_rn(v));
+            }
+        }
+        cluster_sync_all();      // no CTA leaves while a peer still reads its tile
     }
 
     // ---------------- teardown: no MMA may still be writing TMEM when it is freed
@@ -800,8 +846,41 @@ int launch(const Int3TcMaps& maps, const Int3TcParams& p, cudaStream_t stream) {
     const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
     if (st != T4B_OK) return st;
     dim3 grid((p.N + kBN - 1) / kBN, (p.M + kBM - 1) / kBM, p.ksplit);
+    if (p.ksplit > 1 && p.cluster_split) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = (unsigned)p.ksplit;     // the K splits of a tile
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
+        if (e != cudaSuccess) return record_cuda_error(e);
+        return check_launch();
+    }
     kern<<<grid, kThreads, smem, stream>>>(maps, p);
     return check_launch();
+}
+
+}  // namespace
+
+namespace {
+
+// Clusters of `ks` single-CTA INT3 GEMM CTAs resident at once, and the largest
+// split of `tiles` tiles (at most `ks`) whose clusters all are (1: none).
+int cluster_split_of(int tiles, int ks) {
+    static ClusterCapacityCache cache;
+    const int smem = 1024 + kRingBytes + kBarriers * 8 + 16;
+    for (; ks >= 2; --ks)
+        if (tiles <= max_active_clusters(reinterpret_cast<const void*>(gemm_int3_tc_kernel<false, true>), smem,
+                                         kThreads, ks, &cache))
+            return ks;
+    return 1;
 }
 
 }  // namespace
@@ -830,40 +909,46 @@ int gemm_int3_tc(const void* A, const void* W, const void* S, const void* Z, voi
     p.ksteps = (K + kBK - 1) / kBK;
     p.ksplit = 1;
     p.ks_per = p.ksteps;
+    p.cluster_split = 0;
     p.part = nullptr;
     p.counters = nullptr;
-    // M > 128: CTA pairs.  Split K where the tiles (or pairs) leave SMs idle:
-    // for K >= 8192, or for a grid of at most a quarter of the SMs -- pairs
-    // when each split keeps >= 96 K steps, else single CTAs (the INT4 GEMM's
-    // rules, measured there).
+    // M > 128: CTA pairs.  Split K where the tiles (or pairs) leave SMs idle,
+    // by the INT4 GEMM's rules (measured there): K >= 8192 or a grid of at
+    // most a quarter of the SMs from 8 K steps a split, at most half the SMs
+    // from 16; pairs when each split keeps >= 96 K steps, else single CTAs,
+    // whose splits add up in a cluster.
     bool use_pair = M > kBM;
     const int sms = sm_count();
     const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     const int pair_ctas = 2 * ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
+    const bool long_k = K >= kMinSplitK;
+    const bool quarter = 4 * tiles <= sms;
     if (M <= 16) {
         // a decode batch fills one 128-row tile: the dequant of B, which every
         // split shares evenly, is the whole cost, so K splits from 4 K steps a
         // split up to about one CTA per SM (as the FP8 GEMM does)
-        const int ks = std::min(std::min(sms / tiles, p.ksteps / 4), 8);
+        const int ks = cluster_split_of(tiles, std::min(std::min(sms / tiles, p.ksteps / 4), 8));
         if (ks >= 2) {
             p.ks_per = (p.ksteps + ks - 1) / ks;
             p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;
-            Workspace ws;
-            const int st = acquire_workspace(stream, (size_t)tiles, (size_t)tiles * p.ksplit * kBM * kBN, &ws);
-            if (st != T4B_OK) return st;
-            p.part = ws.part;
-            p.counters = ws.counters;
+            p.cluster_split = 1;
         }
-    } else if ((K >= kMinSplitK || 4 * tiles <= sms) && tiles < sms && (!use_pair || pair_ctas < sms)) {
-        auto split_of = [&](int ctas) { return std::min(std::min(sms / ctas, p.ksteps / kMinSplitSteps), 8); };
+    } else if ((long_k || 2 * tiles <= sms) && tiles < sms && (!use_pair || pair_ctas < sms)) {
+        const int min_steps = (long_k || quarter) ? kMinSplitSteps : kMinLooseSplitSteps;
+        auto split_of = [&](int ctas) { return std::min(std::min(sms / ctas, p.ksteps / min_steps), 8); };
         if (use_pair) {
-            const int kp = split_of(pair_ctas);
+            const int kp = (long_k || quarter) ? split_of(pair_ctas) : 1;
             const bool pair_split = kp >= 2 && (p.ksteps + kp - 1) / kp >= kMinPairSplitSteps;
-            if (!pair_split && split_of(tiles) >= 2) use_pair = false;
+            if (!pair_split && cluster_split_of(tiles, split_of(tiles)) >= 2) use_pair = false;
         }
         const int ctas = use_pair ? pair_ctas : tiles;
-        const int ks = split_of(ctas);
-        if (ks >= 2) {
+        const int ks = use_pair ? split_of(ctas) : cluster_split_of(tiles, split_of(tiles));
+        if (ks >= 2 && !use_pair) {
+            // single CTAs: the splits of a tile are one cluster (no workspace)
+            p.ks_per = (p.ksteps + ks - 1) / ks;
+            p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;      // no empty split
+            p.cluster_split = 1;
+        } else if (ks >= 2) {
             p.ks_per = (p.ksteps + ks - 1) / ks;
             p.ksplit = (p.ksteps + p.ks_per - 1) / p.ks_per;      // no empty split
             Workspace ws;

@@ -122,13 +122,6 @@ __device__ __forceinline__ void unpack_natural(uint32_t w, uint32_t (&q)[4]) {
 // Split K in a cluster: a CTA's fp32 tile in shared memory, rows 257 floats apart.
 constexpr int kRedPitch = kBN + 1;
 
-// A 32-bit load from shared memory of a CTA of this cluster (address from mapa).
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
-    return v;
-}
-
 // Per weight format of the single-CTA kernel: INT4 packs 8 K values in a word
 // (8 word rows per K step of 64), FP8-E4M3 4 (16 word rows, a twice larger
 // packed tile, so one TMA stage fewer fits in shared memory).
@@ -835,42 +828,14 @@ int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
 }
 
 // How many clusters of `ks` single-CTA GEMM CTAs can be resident at once on
-// the current device (cached per device and size): a cluster must fit in one
-// GPC, so large clusters of one-CTA-per-SM kernels can fit fewer times than
-// the SM count suggests (measured: 16 clusters of 8 ran in two waves).
+// the current device: a cluster must fit in one GPC, so large clusters of
+// one-CTA-per-SM kernels fit fewer times than the SM count suggests
+// (measured: 16 clusters of 8 ran in two waves).
 int cluster_capacity(int ks) {
-    static std::atomic<int> cached[64][9];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (ks < 2 || ks > 8) return 0;
-    if (dev >= 0 && dev < 64) {
-        const int c = cached[dev][ks].load(std::memory_order_relaxed);
-        if (c > 0) return c - 1;
-    }
     using C = TcCfg<false>;
-    auto kern = gemm_w4_tc_kernel<true, false, false>;
-    const size_t smem = 1024 + (size_t)C::kRingBytes + C::kBarriers * 8 + 16;
-    static SmemLimit limit;
-    int n = 0;
-    if (ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit) == T4B_OK) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(1, 1, (unsigned)ks);
-        cfg.blockDim = dim3(kThreads, 1, 1);
-        cfg.dynamicSmemBytes = smem;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = (unsigned)ks;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
-            cudaGetLastError();
-            n = 0;
-        }
-    }
-    if (dev >= 0 && dev < 64) cached[dev][ks].store(n + 1, std::memory_order_relaxed);
-    return n;
+    static ClusterCapacityCache cache;
+    return max_active_clusters(reinterpret_cast<const void*>(gemm_w4_tc_kernel<true, false, false>),
+                               1024 + C::kRingBytes + C::kBarriers * 8 + 16, kThreads, ks, &cache);
 }
 
 // The largest split of `tiles` single-CTA tiles into clusters of at most `ks`

@@ -91,6 +91,14 @@ __device__ __forceinline__ void tc_mma_pair_f16(uint32_t tmem_d, uint64_t da, ui
         : "memory");
 }
 
+// A 32-bit load from the shared memory of a CTA of this cluster (address from
+// map_to_rank).
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+
 // Arrive on the barrier at cluster address `cluster_addr` once the pair's
 // tcgen05 operations issued before have completed.
 __device__ __forceinline__ void commit_pair(uint32_t cluster_addr) {

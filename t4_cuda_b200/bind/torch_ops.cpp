@@ -21,10 +21,14 @@ namespace {
 
 // t4b_fused_w4a16_gemm_{u4,s4}(A, W, S, Z, C, M, N, K, group, stream)
 using FusedFn = int (*)(const void*, const void*, const void*, const void*, void*, int, int, int, int, void*);
+// t4b_fused_w4a16_gemv_allgather(A, W, S, Z, M, N, K, group, is_signed, gather, stream)
+using AllgatherFn = int (*)(const void*, const void*, const void*, const void*, int, int, int, int, int, const void*,
+                            void*);
 using StatusStringFn = const char* (*)(int);
 using LastCudaErrorFn = int (*)();
 
 FusedFn g_u4 = nullptr, g_s4 = nullptr;
+AllgatherFn g_allgather = nullptr;
 StatusStringFn g_status_string = nullptr;
 LastCudaErrorFn g_last_cuda_error = nullptr;
 PyObject* g_error_class = nullptr;      // t4_cuda_b200._lib.T4BError (a RuntimeError)
@@ -122,15 +126,41 @@ torch::Tensor fused_w4a16_gemm_s4(const torch::Tensor& A, const torch::Tensor& W
     return fused_w4(g_s4, "t4b_fused_w4a16_gemm_s4", A, W, S, Z);
 }
 
+// One call of a fused-gather group (shard.P2PGatherGroup.__call__): the
+// launches of its projections in order, from a table the group builds once --
+// int64 [n, 8]: W, scales, zero points (0: none), N (this rank's columns), K,
+// group size, is_signed, address of the projection's T4BGather.  x: the
+// group's activations, contiguous fp16 [M, K] on the current device.
+void allgather_group(const torch::Tensor& x, const torch::Tensor& table, int64_t M) {
+    if (!g_allgather) fail("t4_cuda_b200 torch binding not initialised");
+    if (!x.is_cuda() || x.scalar_type() != torch::kFloat16 || !x.is_contiguous() || x.dim() != 2 || x.size(0) != M)
+        fail("the fused gather group takes contiguous fp16 activations of " + std::to_string(M) + " rows");
+    if (table.is_cuda() || table.scalar_type() != torch::kInt64 || table.dim() != 2 || table.size(1) != 8 ||
+        !table.is_contiguous())
+        fail("gather table must be a contiguous CPU int64 [n, 8] tensor");
+    const int64_t* t = table.data_ptr<int64_t>();
+    const c10::cuda::CUDAGuard guard(x.device());
+    void* stream = c10::cuda::getCurrentCUDAStream(x.device().index()).stream();
+    const void* a = x.data_ptr();
+    for (int64_t i = 0; i < table.size(0); ++i, t += 8) {
+        const int st = g_allgather(a, reinterpret_cast<const void*>(t[0]), reinterpret_cast<const void*>(t[1]),
+                                   reinterpret_cast<const void*>(t[2]), (int)M, (int)t[3], (int)t[4], (int)t[5],
+                                   (int)t[6], reinterpret_cast<const void*>(t[7]), stream);
+        if (st) raise_status(st, "t4b_fused_w4a16_gemv_allgather");
+    }
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-    m.doc() = "torch binding of t4_cuda_b200's fused W4A16 ops (the hot path of ops.py)";
+    m.doc() = "torch binding of t4_cuda_b200's fused W4A16 ops and fused-gather group calls (the hot paths)";
     m.def(
         "init",
-        [](uintptr_t u4, uintptr_t s4, uintptr_t status_string, uintptr_t last_cuda_error, pybind11::object error_class) {
+        [](uintptr_t u4, uintptr_t s4, uintptr_t allgather, uintptr_t status_string, uintptr_t last_cuda_error,
+           pybind11::object error_class) {
             g_u4 = reinterpret_cast<FusedFn>(u4);
             g_s4 = reinterpret_cast<FusedFn>(s4);
+            g_allgather = reinterpret_cast<AllgatherFn>(allgather);
             g_status_string = reinterpret_cast<StatusStringFn>(status_string);
             g_last_cuda_error = reinterpret_cast<LastCudaErrorFn>(last_cuda_error);
             Py_XDECREF(g_error_class);
@@ -142,4 +172,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("W_packed"), pybind11::arg("scales"), pybind11::arg("zero_points"));
     m.def("fused_w4a16_gemm_s4", &fused_w4a16_gemm_s4, "C = A @ dequant_s4(W_packed)", pybind11::arg("A"),
           pybind11::arg("W_packed"), pybind11::arg("scales"), pybind11::arg("zero_points"));
+    m.def("allgather_group", &allgather_group, "The launches of one fused-gather group call, from its table",
+          pybind11::arg("x"), pybind11::arg("table"), pybind11::arg("M"));
 }

@@ -171,9 +171,10 @@ class P2PGatherGroup:
     t4b_fused_w4a16_gemv_allgather).  With no collective call in it, a step
     made of these groups can be captured as one CUDA graph.
 
-    M is fixed (the buffers are allocated once).  The outputs are views of this
-    rank's output buffer, written only by this rank's own calls, and are
-    overwritten by the group's next call.  Every rank must create its groups
+    M and the projections' tensors are fixed (the buffers are allocated once,
+    and the launches of a call are tabled at construction).  The outputs are
+    views of this rank's output buffer, written only by this rank's own calls,
+    and are overwritten by the group's next call.  Every rank must create its groups
     in the same order and call them in the same order.  Raises RuntimeError
     when the decode kernel does not take a shape (use ShardedGroup, the NCCL
     path, then)."""
@@ -224,6 +225,18 @@ class P2PGatherGroup:
             g.col_offset = self.offsets[i] + self.rank * self.widths[i]
             g.barrier = 1 if i == len(self.linears) - 1 else 0
             self._gathers.append(g)
+        # every call returns the same views of the output buffer; the torch
+        # binding, when built, issues a call's launches from this table
+        self._views = [self.out[:, off:off + self.world * w] for off, w in zip(self.offsets, self.widths)]
+        rows = []
+        for lin, g in zip(self.linears, self._gathers):
+            K = lin.W.size(0) * 8
+            S = lin.S if lin.S.dim() == 2 else lin.S.reshape(1, -1)
+            Z = lin.Z.data_ptr() if lin.Z is not None and lin.Z.numel() else 0
+            rows.append([lin.W.data_ptr(), S.data_ptr(), Z, lin.n_local, K, K // S.size(0),
+                         1 if lin.fmt == "s4" else 0, ctypes.addressof(g)])
+        self._table = torch.tensor(rows, dtype=torch.int64)
+        self._bind = ops._binding()
 
     def _alloc(self, nbytes):
         p = ctypes.c_void_p()
@@ -244,6 +257,9 @@ class P2PGatherGroup:
         return p.value
 
     def __call__(self, x):
+        if self._bind is not None:
+            self._bind.allgather_group(x, self._table, self.M)
+            return self._views
         if x.size(0) != self.M or x.dtype != torch.float16 or not x.is_contiguous():
             raise RuntimeError(f"the fused gather group takes contiguous fp16 activations of {self.M} rows")
         stream = torch._C._cuda_getCurrentRawStream(self.device.index)
@@ -256,7 +272,7 @@ class P2PGatherGroup:
                     1 if lin.fmt == "s4" else 0, ctypes.byref(g), stream)
             if st:
                 _lib.check(st, "t4b_fused_w4a16_gemv_allgather")
-        return [self.out[:, off:off + self.world * w] for off, w in zip(self.offsets, self.widths)]
+        return self._views
 
     def close(self):
         """Release the peers' mappings and this rank's buffers.  Call on every

@@ -216,12 +216,24 @@ struct CtaPlan {
 // 512-word-per-warp stage, so a CTA's stage count is proportional to its tiles
 // (a wide group of 3 tiles idled a quarter of the lanes, a lone narrow tile
 // half of them).  For M > 4 a lone tile is a narrow group of one.
+// First tile of CTA b.  With at least two tiles a CTA, the T mod G tiles left
+// over by the even share go one each to the first CTAs: those are dispatched
+// first and start first, as the previous kernel's CTAs leave their SMs
+// (measured on the decode step: 4096 x 14336 13.1 -> 12.0 us a launch).
+// Below two tiles a CTA the shares are spread evenly (b T / G): there the
+// extra-first order lost (4096 x 4096: 5.3 -> 5.4-5.8 us).
+__device__ __forceinline__ int first_tile(const DecodeParams& p, uint32_t b) {
+    const int base = p.T / p.G;
+    if (base >= 2) return (int)b * base + min((int)b, p.T - base * p.G);
+    return (int)(b * (uint32_t)p.T / (uint32_t)p.G);         // b * T < 2^32 (checked on the host)
+}
+
 template <int MT>
 __device__ __forceinline__ CtaPlan cta_plan(const DecodeParams& p) {
     CtaPlan q;
     const uint32_t b = blockIdx.x;
-    q.t0 = (int)(b * (uint32_t)p.T / (uint32_t)p.G);          // b * T < 2^32 (checked on the host)
-    const int t1 = (int)((b + 1) * (uint32_t)p.T / (uint32_t)p.G);
+    q.t0 = first_tile(p, b);
+    const int t1 = first_tile(p, b + 1);
     const int n = t1 - q.t0;
     q.n4 = n >> 2;
     q.rem = n & 3;

@@ -861,6 +861,7 @@ def run_case(spec, launches=6):
       stream:K:N:M   the same through the split-tile stream kernel
       gemm:M:K:N     s4 group-128 prefill GEMM (tcgen05)
       int3:K:N       H17 INT3 GEMV, M = 1, group 128 (K a multiple of 10)
+      int3gemm:M:K:N H17 INT3 prefill GEMM (tcgen05), group 128
       dequant:KIND:W flat dequant (KIND s4, s3 or fp8; magic mode) of W words"""
     from t4_cuda_b200 import ops
     kind, *dims = spec.split(":")
@@ -888,6 +889,14 @@ def run_case(spec, launches=6):
         Z = torch.empty(0, dtype=torch.float16, device=dev)
         for i in range(launches):
             C = ops.fused_h17_gemv_s3(A, Ws[i % len(Ws)], S, Z, group_size=128)
+    elif kind == "int3gemm":
+        M, K, N = (int(x) for x in dims)
+        W = torch.randint(0, 2 ** 30, (K // 10, N), dtype=torch.int32, device=dev, generator=gen)
+        S = (torch.randn((-(-K // 128), N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half()
+        A = torch.randn((M, K), device=dev, generator=gen).half()
+        Z = torch.empty(0, dtype=torch.float16, device=dev)
+        for _ in range(launches):
+            C = ops.fused_h17_gemv_s3(A, W, S, Z, group_size=128)
     elif kind == "dequant":
         dk, words = dims[0], int(dims[1])
         per = {"s4": 8, "s3": 10, "fp8": 4}[dk]

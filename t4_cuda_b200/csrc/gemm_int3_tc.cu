@@ -285,6 +285,7 @@ gemm_int3_tc_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcParams 
     volatile int* last_flag = abort_flag + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();     // the next kernel may start its prologue as SMs free up
     const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
     const int k_begin = blockIdx.z * p.ks_per;
     const int nsteps = min(p.ks_per, p.ksteps - k_begin);     // >= 1: the host sizes the split so
@@ -319,6 +320,7 @@ gemm_int3_tc_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcParams 
     if (warp == 0) {
         // ---------------- TMA producer: packed words and scale rows
         if (lane == 0) {
+            pdl_wait_prior_grid();   // A may be the previous kernel's output
             for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kStages;
                 if (i >= kStages && !wait_or_abort(&empty[s], (uint32_t)(((i / kStages) & 1) ^ 1), abort_flag)) break;
@@ -352,6 +354,7 @@ gemm_int3_tc_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcParams 
     } else if (warp < kDq0) {
         // ---------------- A loaders: cp.async, kInFlight steps of groups in flight
         const int row0 = 32 * (warp - 2);
+        pdl_wait_prior_grid();       // A may be the previous kernel's output
         int signalled = 0, issued = 0;
         for (int i = 0; i < nsteps; ++i) {
             const int s = i % kStages;
@@ -391,6 +394,7 @@ gemm_int3_tc_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcParams 
             if (lane == 0) mbar_arrive(&full_b[b]);
         }
         // ---------------- epilogue: TMEM lanes 32 * (warp % 4) .. +31 = rows of the tile
+        pdl_wait_prior_grid();       // before any store: the previous kernel may read or write C
         const bool ok = wait_or_abort(acc_full, 0, abort_flag);
         tc_fence_after();
         const int quarter = warp & 3;                       // TMEM lanes this warp may read
@@ -593,6 +597,7 @@ gemm_int3_tc_pair_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcPa
     volatile int* last_flag = abort_flag + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();     // the next kernel may start its prologue as SMs free up
     const uint32_t rank = cluster_rank();            // 0 = leader (issues the MMAs)
     const int pair_id = blockIdx.x >> 1;             // clusters of 2 along x, column tiles fastest
     const int n_tiles = (p.N + kCols - 1) / kCols;
@@ -629,6 +634,7 @@ gemm_int3_tc_pair_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcPa
     if (warp == 0) {
         // ---------------- TMA producer: this CTA's packed words and scale rows
         if (lane == 0) {
+            pdl_wait_prior_grid();   // A may be the previous kernel's output
             for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kStages;
                 if (i >= kStages && !wait_pair(&done[s], (uint32_t)(((i / kStages) & 1) ^ 1), abort_flag)) break;
@@ -664,6 +670,7 @@ gemm_int3_tc_pair_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcPa
     } else if (warp < kDq0) {
         // ---------------- A loaders: this CTA's rows, kInFlight steps of groups in flight
         const int row0 = 32 * (warp - 2);
+        pdl_wait_prior_grid();       // A may be the previous kernel's output
         const uint32_t full_a_leader = map_to_rank(&full_a[0], 0);
         int signalled = 0, issued = 0;
         for (int i = 0; i < nsteps; ++i) {
@@ -708,6 +715,7 @@ gemm_int3_tc_pair_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcPa
             if (lane == 0) arrive_cluster(full_b_leader + (uint32_t)(b * 8));
         }
         // ---------------- epilogue: TMEM lanes 32 * (warp % 4) .. +31 = this CTA's rows
+        pdl_wait_prior_grid();       // before any store: the previous kernel may read or write C
         const bool ok = wait_pair(acc_full, 0, abort_flag);
         tc_fence_after();
         const int quarter = warp & 3;
@@ -824,13 +832,15 @@ int launch(const Int3TcMaps& maps, const Int3TcParams& p, cudaStream_t stream) {
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;      // the two CTAs of an MMA pair are adjacent along x
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // as in the single-CTA launch
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
     if (e != cudaSuccess) return record_cuda_error(e);
     return check_launch();
@@ -846,24 +856,25 @@ int launch(const Int3TcMaps& maps, const Int3TcParams& p, cudaStream_t stream) {
     const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
     if (st != T4B_OK) return st;
     dim3 grid((p.N + kBN - 1) / kBN, (p.M + kBM - 1) / kBM, p.ksplit);
-    if (p.ksplit > 1 && p.cluster_split) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = grid;
-        cfg.blockDim = dim3(kThreads, 1, 1);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = (unsigned)p.ksplit;     // the K splits of a tile
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        return check_launch();
-    }
-    kern<<<grid, kThreads, smem, stream>>>(maps, p);
+    // programmatic dependent launch: the prologue overlaps the previous
+    // kernel's tail (the kernel waits for it before reading A or storing);
+    // the K splits of a tile form one cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = (unsigned)p.ksplit;
+    cfg.attrs = attr;
+    cfg.numAttrs = (p.ksplit > 1 && p.cluster_split) ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
+    if (e != cudaSuccess) return record_cuda_error(e);
     return check_launch();
 }
 

@@ -162,6 +162,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();     // the next kernel may start its prologue as SMs free up
     const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
     const int k_begin = blockIdx.z * p.ks_per;
     const int nsteps = min(p.ks_per, p.ksteps - k_begin);   // >= 1: the host sizes the split so
@@ -197,6 +198,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     if (warp == 0) {
         // ---------------- TMA producer
         if (lane == 0) {
+            pdl_wait_prior_grid();   // A may be the previous kernel's output
             for (int i = 0; i < nsteps; ++i) {
                 const int s = i % C::kTmaStages;
                 const uint32_t ph = (uint32_t)((i / C::kTmaStages) & 1);
@@ -292,6 +294,7 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
             if (lane == 0) mbar_arrive(&full_b[b]);
         }
         // ---------------- epilogue: TMEM lanes 32 * (warp % 4) .. +31 = rows of the tile
+        pdl_wait_prior_grid();       // before any store: the previous kernel may read or write C
         const bool ok = wait_or_abort(acc_full, 0, abort_flag);
         tc_fence_after();
         const int quarter = warp & 3;                       // TMEM lanes this warp may read
@@ -537,6 +540,7 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();     // the next kernel may start its prologue as SMs free up
     const uint32_t rank = cluster_rank();            // 0 = leader (issues the MMAs)
     // 1-D grid of pairs (clusters of 2 along x), column tiles fastest
     const int pair_id = blockIdx.x >> 1;
@@ -576,6 +580,7 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
     if (warp == 0) {
         // ---------------- TMA producer (each CTA loads only its own operands)
         if (lane == 0) {
+            pdl_wait_prior_grid();   // A may be the previous kernel's output
             for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kTmaStages;
                 if (i >= kTmaStages &&
@@ -666,6 +671,7 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
             if (lane == 0) arrive_cluster(full_b_leader + (uint32_t)(b * 8));
         }
         // ---------------- epilogue: TMEM lanes 32 * (warp % 4) .. +31 = this CTA's rows
+        pdl_wait_prior_grid();       // before any store: the previous kernel may read or write C
         const bool ok = wait_pair(acc_full, 0, abort_flag);
         tc_fence_after();
         const int quarter = warp & 3;
@@ -782,13 +788,15 @@ int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;      // the two CTAs of an MMA pair are adjacent along x
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // as in the single-CTA launch
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
     if (e != cudaSuccess) return record_cuda_error(e);
     return check_launch();
@@ -805,25 +813,25 @@ int launch(const GemmMaps& maps, const GemmParams& p, cudaStream_t stream) {
     const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
     if (st != T4B_OK) return st;
     dim3 grid((p.N + kBN - 1) / kBN, (p.M + kBM - 1) / kBM, p.ksplit);
-    if (p.ksplit > 1 && p.cluster_split) {
-        // the K splits of a tile form one cluster (at most 8 CTAs)
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = grid;
-        cfg.blockDim = dim3(kThreads, 1, 1);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = (unsigned)p.ksplit;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
-        if (e != cudaSuccess) return record_cuda_error(e);
-        return check_launch();
-    }
-    kern<<<grid, kThreads, smem, stream>>>(maps, p);
+    // programmatic dependent launch: the prologue overlaps the previous
+    // kernel's tail (the kernel waits for it before reading A or storing);
+    // the K splits of a tile form one cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = (unsigned)p.ksplit;
+    cfg.attrs = attr;
+    cfg.numAttrs = (p.ksplit > 1 && p.cluster_split) ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
+    if (e != cudaSuccess) return record_cuda_error(e);
     return check_launch();
 }
 

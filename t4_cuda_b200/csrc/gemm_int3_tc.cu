@@ -320,7 +320,8 @@ gemm_int3_tc_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcParams 
     if (warp == 0) {
         // ---------------- TMA producer: packed words and scale rows
         if (lane == 0) {
-            pdl_wait_prior_grid();   // A may be the previous kernel's output
+            // packed words and scales only: never written by a kernel of this
+            // library, so no dependency wait (the A loaders wait)
             for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kStages;
                 if (i >= kStages && !wait_or_abort(&empty[s], (uint32_t)(((i / kStages) & 1) ^ 1), abort_flag)) break;
@@ -634,7 +635,8 @@ gemm_int3_tc_pair_kernel(const __grid_constant__ Int3TcMaps maps, const Int3TcPa
     if (warp == 0) {
         // ---------------- TMA producer: this CTA's packed words and scale rows
         if (lane == 0) {
-            pdl_wait_prior_grid();   // A may be the previous kernel's output
+            // packed words and scales only: never written by a kernel of this
+            // library, so no dependency wait (the A loaders wait)
             for (int i = 0; i < nsteps; ++i) {
                 const int s = i % kStages;
                 if (i >= kStages && !wait_pair(&done[s], (uint32_t)(((i / kStages) & 1) ^ 1), abort_flag)) break;

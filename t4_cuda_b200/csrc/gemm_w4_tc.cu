@@ -198,20 +198,35 @@ gemm_w4_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
     if (warp == 0) {
         // ---------------- TMA producer
         if (lane == 0) {
-            pdl_wait_prior_grid();   // A may be the previous kernel's output
-            for (int i = 0; i < nsteps; ++i) {
+            // Packed words, scales and zero points are never written by a
+            // kernel of this library, so the first ring stages' copies of them
+            // go out before the dependency wait on the previous kernel; A's
+            // (which that kernel may have written) after it.
+            auto weights = [&](int i) {
                 const int s = i % C::kTmaStages;
-                const uint32_t ph = (uint32_t)((i / C::kTmaStages) & 1);
-                if (i >= C::kTmaStages && !wait_or_abort(&empty_tma[s], ph ^ 1u, abort_flag)) break;
                 uint8_t* st = base + s * C::kTmaStageBytes;
                 const int kg = k_begin + i;                         // K step in the whole of K
                 const int srow = p.gw_steps ? kg / p.gw_steps : 0;
                 mbar_arrive_expect_tx(&full_tma[s], kABytes + C::kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
-                tma_load_2d(st, &maps.a, kg * kBK, m0, &full_tma[s]);
                 tma_load_2d(st + kABytes, &maps.w, n0, kg * C::kWordRows, &full_tma[s]);
                 tma_load_2d(st + kABytes + C::kWBytes, &maps.s, n0, srow, &full_tma[s]);
                 if constexpr (HAS_ZP)
                     tma_load_2d(st + kABytes + C::kWBytes + kSBytes, &maps.z, n0, srow, &full_tma[s]);
+            };
+            auto act = [&](int i) {
+                const int s = i % C::kTmaStages;
+                tma_load_2d(base + s * C::kTmaStageBytes, &maps.a, (k_begin + i) * kBK, m0, &full_tma[s]);
+            };
+            const int pre = min(nsteps, C::kTmaStages);
+            for (int i = 0; i < pre; ++i) weights(i);
+            pdl_wait_prior_grid();   // A may be the previous kernel's output
+            for (int i = 0; i < pre; ++i) act(i);
+            for (int i = pre; i < nsteps; ++i) {
+                const int s = i % C::kTmaStages;
+                const uint32_t ph = (uint32_t)((i / C::kTmaStages) & 1);
+                if (!wait_or_abort(&empty_tma[s], ph ^ 1u, abort_flag)) break;
+                weights(i);
+                act(i);
             }
         }
     } else if (warp == 1) {
@@ -580,21 +595,31 @@ gemm_w4_tc_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p
     if (warp == 0) {
         // ---------------- TMA producer (each CTA loads only its own operands)
         if (lane == 0) {
-            pdl_wait_prior_grid();   // A may be the previous kernel's output
-            for (int i = 0; i < nsteps; ++i) {
+            // the weights of the first ring stages before the dependency wait,
+            // A after it (as in the single-CTA kernel)
+            auto weights = [&](int i) {
                 const int s = i % kTmaStages;
-                if (i >= kTmaStages &&
-                    !wait_pair(&done[s], (uint32_t)(((i / kTmaStages) & 1) ^ 1), abort_flag))
-                    break;
                 uint8_t* st = base + s * kStageBytes;
                 const int kg = k_begin + i;                         // K step in the whole of K
                 const int srow = p.gw_steps ? kg / p.gw_steps : 0;
                 mbar_arrive_expect_tx(&full_tma[s], kABytes + kWBytes + kSBytes * (HAS_ZP ? 2 : 1));
-                tma_load_2d(st, &maps.a, kg * kBK, m0, &full_tma[s]);
                 tma_load_2d(st + kABytes, &maps.w, nh, kg * (kBK / 8), &full_tma[s]);
                 tma_load_2d(st + kABytes + kWBytes, &maps.s, nh, srow, &full_tma[s]);
                 if constexpr (HAS_ZP)
                     tma_load_2d(st + kABytes + kWBytes + kSBytes, &maps.z, nh, srow, &full_tma[s]);
+            };
+            auto act = [&](int i) {
+                const int s = i % kTmaStages;
+                tma_load_2d(base + s * kStageBytes, &maps.a, (k_begin + i) * kBK, m0, &full_tma[s]);
+            };
+            const int pre = min(nsteps, kTmaStages);
+            for (int i = 0; i < pre; ++i) weights(i);
+            pdl_wait_prior_grid();   // A may be the previous kernel's output
+            for (int i = 0; i < pre; ++i) act(i);
+            for (int i = pre; i < nsteps; ++i) {
+                if (!wait_pair(&done[i % kTmaStages], (uint32_t)(((i / kTmaStages) & 1) ^ 1), abort_flag)) break;
+                weights(i);
+                act(i);
             }
         }
     } else if (warp == 1) {

@@ -261,6 +261,10 @@ gemv_int3_kernel(const Int3Params p) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[mt][t][i] = 0.f;
 
+    // programmatic dependent launch: the next kernel may start as SMs free up;
+    // this one reads A and writes C only after the previous kernel is done
+    pdl_launch_dependents();
+    pdl_wait_prior_grid();
     Int3Step<MT, HAS_ZP> buf[kNB];
 #pragma unroll
     for (int i = 0; i < kNB; ++i)
@@ -650,22 +654,21 @@ template <int MT, bool HAS_ZP, bool VEC>
 int launch(const Int3Params& p, int splits, cudaStream_t stream) {
     const dim3 block(kWarps * 32);
     const dim3 grid((p.N + kTileN - 1) / kTileN, splits, (p.M + 8 * MT - 1) / (8 * MT));
-    if (splits == 1) {
-        gemv_int3_kernel<MT, HAS_ZP, VEC, false><<<grid, block, 0, stream>>>(p);
-        return check_launch();
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = splits;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;       // K split over a cluster (DSMEM reduction)
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = splits;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, gemv_int3_kernel<MT, HAS_ZP, VEC, true>, p);
+    cfg.numAttrs = splits > 1 ? 2 : 1;
+    cudaError_t err = splits > 1 ? cudaLaunchKernelEx(&cfg, gemv_int3_kernel<MT, HAS_ZP, VEC, true>, p)
+                                 : cudaLaunchKernelEx(&cfg, gemv_int3_kernel<MT, HAS_ZP, VEC, false>, p);
     if (err != cudaSuccess) return record_cuda_error(err);
     return check_launch();
 }

@@ -569,7 +569,15 @@ def run_ours(args):
         return outs
 
     step_bytes = N_LAYERS * sum(alg_bytes(M, K, N) for _, K, N in PROJ)
-    launches_per_step = N_LAYERS * len(PROJ)
+    # one launch per projection, or one per group where ShardedGroup makes a
+    # grouped call that the decode kernel takes as one launch
+    def group_launches(grp, act, names):
+        if getattr(grp, "_grouped", None) is None:
+            return len(names)
+        Ns = [N // world for n, _, N in PROJ if n in names]
+        return 1 if ops.grouped_plan(Ns, M, ACT_K[act], GROUP) is not None else len(names)
+    launches_per_step = N_LAYERS * sum(group_launches(pg_layers[0][g], a, names)
+                                       for g, (a, names) in enumerate(GATHERS))
 
     use_graph = gather_mode in ("single GPU", "fused")
     if use_graph:
@@ -619,6 +627,35 @@ def run_ours(args):
         ms = float(t.item())
     ms_per_step = ms / args.steps
     value = step_bytes * args.steps / (ms * 1e-3) / 1e9
+
+    # ---- the same step through the reference's op surface: one
+    # fused_w4a16_gemm_s4 call per projection (one GPU, a CUDA graph)
+    per_proj = None
+    if world == 1:
+        def token_single(act):
+            outs = []
+            for li in range(N_LAYERS):
+                groups = pg_layers[li % pool]
+                for g, (a, names) in enumerate(GATHERS):
+                    outs.extend(lin.local(act[a]) for lin in groups[g].linears)
+            return outs
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            token_single(acts)
+        for _ in range(args.warmup):
+            g1.replay()
+        torch.cuda.synchronize()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        for _ in range(args.steps):
+            g1.replay()
+        p1.record()
+        p1.synchronize()
+        pms = p0.elapsed_time(p1) / args.steps
+        per_proj = {"ms_per_step": round(pms, 4), "GB/s": round(step_bytes / (pms * 1e-3) / 1e9, 1),
+                    "launches_per_step": N_LAYERS * len(PROJ),
+                    "api": "fused_w4a16_gemm_s4, one call per projection (the reference's op surface)"}
+        del g1
 
     # ---- per-shape breakdown (one GPU): a graph of `pool` launches of one shape
     per_shape = {}
@@ -688,6 +725,35 @@ def run_ours(args):
         e2e_ms = float(t.item())
     e2e_value = step_bytes * args.steps / (e2e_ms * 1e-3) / 1e9
 
+    # ---- the same end to end through the drop-in op, one call per projection
+    e2e_single = None
+    if world == 1:
+        import t4_kernels
+
+        def e2e_step_single():
+            for a in acts:
+                dev_in[a].copy_(pin[a], non_blocking=True)
+            outs = []
+            for li in range(N_LAYERS):
+                L = layers[li % pool]
+                for name, K, N in PROJ:
+                    a = "h" if name == "down" else ("attn" if name == "o" else "x")
+                    outs.append(t4_kernels.fused_w4a16_gemm_s4(dev_in[a], L[name][0], L[name][1], None))
+            out_host.copy_(torch.cat([o.reshape(-1) for o in outs]), non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step_single()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step_single()
+        e1.record()
+        e1.synchronize()
+        sms = e0.elapsed_time(e1) / args.steps
+        e2e_single = {"value": round(step_bytes / (sms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(sms, 4),
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                      "api": "t4_kernels.fused_w4a16_gemm_s4, one call per projection (eager, pinned host buffers)"}
+
     # a bounded wait that ran out or a launch that aborted sets the library's
     # device error word; the line reports it (max over ranks)
     dev_err = int(ops.device_error(dev))
@@ -754,11 +820,14 @@ def run_ours(args):
         "device_error": dev_err,
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
-                "api": {"single GPU": "t4_kernels.fused_w4a16_gemm_s4",
+                "api": {"single GPU": "t4_cuda_b200.shard.ShardedGroup: fused_w4a16_gemm_grouped for q/k/v and "
+                                      "gate/up, fused_w4a16_gemm_s4 for o and down",
                         "fused": "t4_cuda_b200.shard.P2PGatherGroup (t4b_fused_w4a16_gemv_allgather)",
                         "nccl": "t4_cuda_b200.shard.ShardedGroup"}[gather_mode] + " (eager, pinned host buffers)"},
         "per_shape": per_shape,
         "roofline": roof,
+        "per_projection_step": per_proj,
+        "e2e_per_projection": e2e_single,
         "clocks": clk.summary(),
     }
     if gemm is not None:

@@ -140,6 +140,29 @@ int t4b_fused_w4a16_gemm_s4(const void* A, const void* W_packed, const void* sca
                             const void* zero_points, void* C, int M, int N, int K,
                             int group_size, void* stream);
 
+/* Projections that read the same activation, in one call: C[j] (f16
+ * [M, N[j]]) = A x dequant(W_packed[j]) for j < n (1 <= n <= T4B_GROUPED_MAX),
+ * all with the same K, group_size and signedness (is_signed: s4, else u4).
+ * zero_points is NULL (no zero points) or n pointers, all set.  No
+ * counterpart in the reference, whose op takes one projection (a layer's
+ * q/k/v or gate/up are n calls of fused_w4a16_gemm_{u4,s4}); the results
+ * match those n calls within the ops' tolerance.  Where the decode kernel
+ * takes the shapes (M <= 16 under T4B_GEMV_AUTO / TC_SINGLE) the projections
+ * run as one launch whose CTAs are shared out by column tiles; otherwise the
+ * call makes the n single calls itself. */
+#define T4B_GROUPED_MAX 4
+int t4b_fused_w4a16_gemm_grouped(const void* A, int n, const void* const* W_packed,
+                                 const void* const* scales, const void* const* zero_points,
+                                 void* const* C, const int* N, int M, int K, int group_size,
+                                 int is_signed, void* stream);
+
+/* T4B_OK and the CTAs of each projection (ctas[j], j < n) of the one launch
+ * t4b_fused_w4a16_gemm_grouped makes for these shapes, or T4B_ERR_UNSUPPORTED
+ * when it would make single calls instead; launches nothing, but reads the
+ * current device's SM count. */
+int t4b_fused_w4a16_gemm_grouped_plan(int n, const int* N, int M, int K, int group_size,
+                                      int has_zero_points, int* ctas);
+
 /* FP8-E4M3 weight GEMM.  No counterpart in the reference, which has only the
  * flat dequantizer of this format (launch_lop3_dequant_fp8,
  * src/kernels/lop3_dequant.h:135-136): the fused path for it.

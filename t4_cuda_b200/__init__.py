@@ -16,6 +16,7 @@ from .ops import (  # noqa: F401
     dequantize_fp8,
     fused_w4a16_gemm_u4,
     fused_w4a16_gemm_s4,
+    fused_w4a16_gemm_grouped,
     fused_h17_gemv_s3,
     fused_w8a16_gemm_fp8,
     set_gemv_kernel,

@@ -22,6 +22,8 @@ SIGNATURES = {
     "t4b_dequantize_fp8": [_vp, _vp, _vp, _i64, _i64, _i32, _vp],
     "t4b_fused_w4a16_gemm_u4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_w4a16_gemm_s4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
+    "t4b_fused_w4a16_gemm_grouped": [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
+    "t4b_fused_w4a16_gemm_grouped_plan": [_i32, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_h17_gemv_s3": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_w8a16_gemm_fp8": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_w4a16_gemv_noalloc": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp],

@@ -16,6 +16,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 namespace {
 
@@ -24,11 +25,15 @@ using FusedFn = int (*)(const void*, const void*, const void*, const void*, void
 // t4b_fused_w4a16_gemv_allgather(A, W, S, Z, M, N, K, group, is_signed, gather, stream)
 using AllgatherFn = int (*)(const void*, const void*, const void*, const void*, int, int, int, int, int, const void*,
                             void*);
+// t4b_fused_w4a16_gemm_grouped(A, n, W[], S[], Z[], C[], N[], M, K, group, is_signed, stream)
+using GroupedFn = int (*)(const void*, int, const void* const*, const void* const*, const void* const*, void* const*,
+                          const int*, int, int, int, int, void*);
 using StatusStringFn = const char* (*)(int);
 using LastCudaErrorFn = int (*)();
 
 FusedFn g_u4 = nullptr, g_s4 = nullptr;
 AllgatherFn g_allgather = nullptr;
+GroupedFn g_grouped = nullptr;
 StatusStringFn g_status_string = nullptr;
 LastCudaErrorFn g_last_cuda_error = nullptr;
 PyObject* g_error_class = nullptr;      // t4_cuda_b200._lib.T4BError (a RuntimeError)
@@ -76,11 +81,14 @@ torch::Tensor aligned16(const torch::Tensor& t) {
 
 bool has_values(const c10::optional<torch::Tensor>& z) { return z.has_value() && z->defined() && z->numel() > 0; }
 
-// ops._fused: C = A @ dequant_w4(W_packed), bindings.cpp:64-132.
-torch::Tensor fused_w4(FusedFn fn, const char* name, const torch::Tensor& A, const torch::Tensor& W,
-                       const torch::Tensor& S, const c10::optional<torch::Tensor>& Zopt) {
-    if (!fn) fail("t4_cuda_b200 torch binding not initialised");
-    if (!A.is_cuda()) fail("A must be a CUDA tensor");
+struct WShape {
+    int64_t M, N, K, G;
+    bool has_zp;
+};
+
+// ops._check_w: the checks of bindings.cpp:64-132 after A's device check.
+WShape check_w(const torch::Tensor& A, const torch::Tensor& W, const torch::Tensor& S,
+               const c10::optional<torch::Tensor>& Zopt) {
     if (!W.is_cuda()) fail("W_packed must be a CUDA tensor");
     if (!S.is_cuda()) fail("scales must be a CUDA tensor");
     const bool has_zp = has_values(Zopt);
@@ -103,16 +111,83 @@ torch::Tensor fused_w4(FusedFn fn, const char* name, const torch::Tensor& A, con
         fail("W_packed must have K/8=" + std::to_string(K / 8) + " rows, got " + std::to_string(W.size(0)));
     const int64_t G = group_rows(S, N, K, "scales", 8);
     if (has_zp && group_rows(*Zopt, N, K, "zero_points", 8) != G) fail("zero_points must have the same shape as scales");
+    return {M, N, K, G, has_zp};
+}
+
+torch::Tensor contig(const torch::Tensor& t) { return t.is_contiguous() ? t : t.contiguous(); }
+
+// ops._fused: C = A @ dequant_w4(W_packed), bindings.cpp:64-132.
+torch::Tensor fused_w4(FusedFn fn, const char* name, const torch::Tensor& A, const torch::Tensor& W,
+                       const torch::Tensor& S, const c10::optional<torch::Tensor>& Zopt) {
+    if (!fn) fail("t4_cuda_b200 torch binding not initialised");
+    if (!A.is_cuda()) fail("A must be a CUDA tensor");
+    const WShape w = check_w(A, W, S, Zopt);
     const torch::Tensor A_ = aligned16(A);
-    const torch::Tensor W_ = W.is_contiguous() ? W : W.contiguous();
-    const torch::Tensor S_ = S.is_contiguous() ? S : S.contiguous();
+    const torch::Tensor W_ = contig(W);
+    const torch::Tensor S_ = contig(S);
     torch::Tensor Z_;
-    if (has_zp) Z_ = Zopt->is_contiguous() ? *Zopt : Zopt->contiguous();
+    if (w.has_zp) Z_ = contig(*Zopt);
+    const auto dev = A.device();
     const c10::cuda::CUDAGuard guard(dev);
-    torch::Tensor C = torch::empty({M, N}, A.options());
-    const int st = fn(A_.data_ptr(), W_.data_ptr(), S_.data_ptr(), has_zp ? Z_.data_ptr() : nullptr, C.data_ptr(),
-                      (int)M, (int)N, (int)K, (int)(K / G), c10::cuda::getCurrentCUDAStream(dev.index()).stream());
+    torch::Tensor C = torch::empty({w.M, w.N}, A.options());
+    const int st = fn(A_.data_ptr(), W_.data_ptr(), S_.data_ptr(), w.has_zp ? Z_.data_ptr() : nullptr, C.data_ptr(),
+                      (int)w.M, (int)w.N, (int)w.K, (int)(w.K / w.G),
+                      c10::cuda::getCurrentCUDAStream(dev.index()).stream());
     if (st) raise_status(st, name);
+    return C;
+}
+
+constexpr int kGroupedMax = 4;      // T4B_GROUPED_MAX
+
+// ops._fused_grouped: the projections of W_list that read A, in one call.
+std::vector<torch::Tensor> fused_w4a16_gemm_grouped(const torch::Tensor& A, const std::vector<torch::Tensor>& Ws,
+                                                    const std::vector<torch::Tensor>& Ss,
+                                                    const c10::optional<std::vector<c10::optional<torch::Tensor>>>& Zs,
+                                                    bool is_signed) {
+    if (!g_grouped) fail("t4_cuda_b200 torch binding not initialised");
+    const int n = (int)Ws.size();
+    if (n < 1 || n > kGroupedMax)
+        fail("a grouped call takes 1 to " + std::to_string(kGroupedMax) + " projections, got " + std::to_string(n));
+    if ((int)Ss.size() != n || (Zs.has_value() && (int)Zs->size() != n))
+        fail("W_packed, scales and zero_points lists must have the same length");
+    if (!A.is_cuda()) fail("A must be a CUDA tensor");
+    WShape w[kGroupedMax];
+    for (int j = 0; j < n; ++j) {
+        const c10::optional<torch::Tensor> z = Zs.has_value() ? (*Zs)[j] : c10::nullopt;
+        w[j] = check_w(A, Ws[j], Ss[j], z);
+    }
+    for (int j = 1; j < n; ++j)
+        if (w[j].G != w[0].G) fail("every projection of a grouped call must have the same group size");
+    for (int j = 1; j < n; ++j)
+        if (w[j].has_zp != w[0].has_zp)
+            fail("zero_points must be given for every projection of a grouped call or for none");
+    const bool has_zp = w[0].has_zp;
+    const torch::Tensor A_ = aligned16(A);
+    torch::Tensor W_[kGroupedMax], S_[kGroupedMax], Z_[kGroupedMax];
+    const void *wp[kGroupedMax], *sp[kGroupedMax], *zp[kGroupedMax];
+    void* cp[kGroupedMax];
+    int Ns[kGroupedMax];
+    const auto dev = A.device();
+    const c10::cuda::CUDAGuard guard(dev);
+    std::vector<torch::Tensor> C;
+    C.reserve(n);
+    for (int j = 0; j < n; ++j) {
+        W_[j] = contig(Ws[j]);
+        S_[j] = contig(Ss[j]);
+        wp[j] = W_[j].data_ptr();
+        sp[j] = S_[j].data_ptr();
+        if (has_zp) {
+            Z_[j] = contig(*(*Zs)[j]);
+            zp[j] = Z_[j].data_ptr();
+        }
+        C.push_back(torch::empty({w[j].M, w[j].N}, A.options()));
+        cp[j] = C.back().data_ptr();
+        Ns[j] = (int)w[j].N;
+    }
+    const int st = g_grouped(A_.data_ptr(), n, wp, sp, has_zp ? zp : nullptr, cp, Ns, (int)w[0].M, (int)w[0].K,
+                             (int)(w[0].K / w[0].G), is_signed ? 1 : 0,
+                             c10::cuda::getCurrentCUDAStream(dev.index()).stream());
+    if (st) raise_status(st, "t4b_fused_w4a16_gemm_grouped");
     return C;
 }
 
@@ -156,11 +231,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "torch binding of t4_cuda_b200's fused W4A16 ops and fused-gather group calls (the hot paths)";
     m.def(
         "init",
-        [](uintptr_t u4, uintptr_t s4, uintptr_t allgather, uintptr_t status_string, uintptr_t last_cuda_error,
-           pybind11::object error_class) {
+        [](uintptr_t u4, uintptr_t s4, uintptr_t allgather, uintptr_t grouped, uintptr_t status_string,
+           uintptr_t last_cuda_error, pybind11::object error_class) {
             g_u4 = reinterpret_cast<FusedFn>(u4);
             g_s4 = reinterpret_cast<FusedFn>(s4);
             g_allgather = reinterpret_cast<AllgatherFn>(allgather);
+            g_grouped = reinterpret_cast<GroupedFn>(grouped);
             g_status_string = reinterpret_cast<StatusStringFn>(status_string);
             g_last_cuda_error = reinterpret_cast<LastCudaErrorFn>(last_cuda_error);
             Py_XDECREF(g_error_class);
@@ -172,6 +248,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("W_packed"), pybind11::arg("scales"), pybind11::arg("zero_points"));
     m.def("fused_w4a16_gemm_s4", &fused_w4a16_gemm_s4, "C = A @ dequant_s4(W_packed)", pybind11::arg("A"),
           pybind11::arg("W_packed"), pybind11::arg("scales"), pybind11::arg("zero_points"));
+    m.def("fused_w4a16_gemm_grouped", &fused_w4a16_gemm_grouped,
+          "[A @ dequant(W) for W in W_list]: projections that read the same activation, in one call",
+          pybind11::arg("A"), pybind11::arg("W_list"), pybind11::arg("scales_list"),
+          pybind11::arg("zero_points_list"), pybind11::arg("is_signed"));
     m.def("allgather_group", &allgather_group, "The launches of one fused-gather group call, from its table",
           pybind11::arg("x"), pybind11::arg("table"), pybind11::arg("M"));
 }

@@ -55,6 +55,14 @@ int gemv_w4_decode_supported(int M, int N, int K, int group, bool has_zero_point
 // decode kernel does not apply.
 int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const void* S, const void* Z, int M, int N,
                           int K, int group, const T4BGather* g, cudaStream_t stream);
+// One decode launch for np projections that read the same A (W, S, C, N:
+// np entries each; Z NULL or np entries); T4B_ERR_UNSUPPORTED (nothing
+// launched) where the decode kernel does not take the shapes.
+int gemv_w4_decode_grouped(bool is_signed, const void* A, int np, const void* const* W, const void* const* S,
+                           const void* const* Z, void* const* C, const int* N, int M, int K, int group,
+                           cudaStream_t stream);
+// The CTAs of each projection of that launch (nothing is launched).
+int gemv_w4_decode_grouped_plan(int np, const int* N, int M, int K, int group, bool has_zero_points, int* ctas);
 
 // Reads (and optionally clears) the decode GEMV's device error word on the
 // current device; synchronizes `stream`.

@@ -322,10 +322,62 @@ int fused_gemm(const void* A, const void* W, const void* S, const void* Z, void*
     return Z ? dispatch_vec<2, SIGNED, true>(p, vec, splits, s) : dispatch_vec<2, SIGNED, false>(p, vec, splits, s);
 }
 
+// Argument checks of one projection of a grouped call, as fused_gemm's.
+int check_grouped(const void* A, int n, const void* const* W, const void* const* S, const void* const* Z,
+                  void* const* C, const int* N, int M, int K, int group) {
+    if (n < 1 || n > T4B_GROUPED_MAX || M < 1 || K < 8 || (K % 8) != 0) return T4B_ERR_INVALID_VALUE;
+    if (group < 8 || (group % 8) != 0 || (K % group) != 0) return T4B_ERR_INVALID_VALUE;
+    if (!A || !W || !S || !C || !N) return T4B_ERR_NULL_POINTER;
+    if (!aligned(A, 16)) return T4B_ERR_MISALIGNED;
+    for (int j = 0; j < n; ++j) {
+        if (N[j] < 1) return T4B_ERR_INVALID_VALUE;
+        if (!W[j] || !S[j] || !C[j] || (Z && !Z[j])) return T4B_ERR_NULL_POINTER;
+        if (!aligned(W[j], 4) || !aligned(S[j], 2) || !aligned(C[j], 2) || (Z && !aligned(Z[j], 2)))
+            return T4B_ERR_MISALIGNED;
+    }
+    return T4B_OK;
+}
+
+template <bool SIGNED>
+int fused_grouped(const void* A, int n, const void* const* W, const void* const* S, const void* const* Z,
+                  void* const* C, const int* N, int M, int K, int group, void* stream_) {
+    const int st = check_grouped(A, n, W, S, Z, C, N, M, K, group);
+    if (st != T4B_OK) return st;
+    const int choice = g_gemv_kernel.load();
+    if ((choice == T4B_GEMV_AUTO || choice == T4B_GEMV_TC_SINGLE) && M <= kStreamMaxM) {
+        const int g = gemv_w4_decode_grouped(SIGNED, A, n, W, S, Z, C, N, M, K, group,
+                                             static_cast<cudaStream_t>(stream_));
+        if (g != T4B_ERR_UNSUPPORTED) return g;
+    }
+    for (int j = 0; j < n; ++j) {
+        const int s = fused_gemm<SIGNED>(A, W[j], S[j], Z ? Z[j] : nullptr, C[j], M, N[j], K, group, stream_);
+        if (s != T4B_OK) return s;
+    }
+    return T4B_OK;
+}
+
 }  // namespace
 }  // namespace t4b
 
 extern "C" {
+
+int t4b_fused_w4a16_gemm_grouped(const void* A, int n, const void* const* W_packed, const void* const* scales,
+                                 const void* const* zero_points, void* const* C, const int* N, int M, int K,
+                                 int group_size, int is_signed, void* stream) {
+    return is_signed ? t4b::fused_grouped<true>(A, n, W_packed, scales, zero_points, C, N, M, K, group_size, stream)
+                     : t4b::fused_grouped<false>(A, n, W_packed, scales, zero_points, C, N, M, K, group_size, stream);
+}
+
+int t4b_fused_w4a16_gemm_grouped_plan(int n, const int* N, int M, int K, int group_size, int has_zero_points,
+                                      int* ctas) {
+    if (n < 1 || n > T4B_GROUPED_MAX || M < 1 || K < 8 || (K % 8) != 0) return T4B_ERR_INVALID_VALUE;
+    if (group_size < 8 || (group_size % 8) != 0 || (K % group_size) != 0) return T4B_ERR_INVALID_VALUE;
+    if (!N || !ctas) return T4B_ERR_NULL_POINTER;
+    for (int j = 0; j < n; ++j)
+        if (N[j] < 1) return T4B_ERR_INVALID_VALUE;
+    if (M > t4b::kStreamMaxM) return T4B_ERR_UNSUPPORTED;
+    return t4b::gemv_w4_decode_grouped_plan(n, N, M, K, group_size, has_zero_points != 0, ctas);
+}
 
 int t4b_set_gemv_kernel(int which) {
     if (which != T4B_GEMV_AUTO && which != T4B_GEMV_GENERIC && which != T4B_GEMV_STREAM && which != T4B_GEMV_TC_SINGLE)

@@ -61,6 +61,7 @@ namespace {
 
 constexpr int kBoxCols = 16;                       // columns per TMA box (64 bytes)
 constexpr int kMaxStages = 12;
+constexpr int kMaxProj = T4B_GROUPED_MAX;          // projections of one grouped launch
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr unsigned kErrTimeout = 1u;
 
@@ -102,6 +103,15 @@ struct DecodeParams {
     int sum_floats;     // flush-block activation sums
     int red_floats;     // cross-warp reduction buffer
     FastDiv kwdiv;      // division by KWp
+    // Projections of this launch (one, or a group that shares A): projection
+    // j owns CTAs [proj_g0[j], proj_g0[j+1]) and its T = proj_T[j] tiles,
+    // output proj_C[j] of proj_N[j] columns.  T, G, N and C above are those of
+    // a one-projection launch.
+    int nproj;
+    int proj_g0[kMaxProj + 1];
+    int proj_T[kMaxProj];
+    int proj_N[kMaxProj];
+    uint16_t* proj_C[kMaxProj];
     // fused all-gather (world > 1): each pair of output columns goes, with the
     // call's epoch, as one 64-bit word to every rank's receive buffer
     unsigned long long* recv[8];
@@ -110,7 +120,8 @@ struct DecodeParams {
     int world, rank, n_total, col_offset, barrier;
 };
 
-struct DecodeMaps {
+// Tensor maps of one projection.
+struct ProjMaps {
     CUtensorMap w_wide;     // packed words, box 16 columns x rows_wide
     CUtensorMap w_narrow;   // packed words, box 16 columns x rows_narrow
     CUtensorMap s_wide;     // scales, box 64 columns x sbr_wide rows
@@ -119,6 +130,11 @@ struct DecodeMaps {
     CUtensorMap z_narrow;
     CUtensorMap s_split;    // scales, box 16 columns x sbr_split rows
     CUtensorMap z_split;
+};
+
+template <int NP>
+struct DecodeMaps {
+    ProjMaps proj[NP];
 };
 
 // A pure function of its operands (not volatile), so the compiler may
@@ -222,18 +238,18 @@ struct CtaPlan {
 // (measured on the decode step: 4096 x 14336 13.1 -> 12.0 us a launch).
 // Below two tiles a CTA the shares are spread evenly (b T / G): there the
 // extra-first order lost (4096 x 4096: 5.3 -> 5.4-5.8 us).
-__device__ __forceinline__ int first_tile(const DecodeParams& p, uint32_t b) {
-    const int base = p.T / p.G;
-    if (base >= 2) return (int)b * base + min((int)b, p.T - base * p.G);
-    return (int)(b * (uint32_t)p.T / (uint32_t)p.G);         // b * T < 2^32 (checked on the host)
+// T tiles over G CTAs (of one projection).
+__device__ __forceinline__ int first_tile(int T, int G, uint32_t b) {
+    const int base = T / G;
+    if (base >= 2) return (int)b * base + min((int)b, T - base * G);
+    return (int)(b * (uint32_t)T / (uint32_t)G);         // b * T < 2^32 (checked on the host)
 }
 
-template <int MT>
-__device__ __forceinline__ CtaPlan cta_plan(const DecodeParams& p) {
+// Tiles and stages of CTA b of the G that share the T tiles of a projection.
+__device__ __forceinline__ CtaPlan cta_plan(const DecodeParams& p, int T, int G, uint32_t b) {
     CtaPlan q;
-    const uint32_t b = blockIdx.x;
-    q.t0 = first_tile(p, b);
-    const int t1 = first_tile(p, b + 1);
+    q.t0 = first_tile(T, G, b);
+    const int t1 = first_tile(T, G, b + 1);
     const int n = t1 - q.t0;
     q.n4 = n >> 2;
     q.rem = n & 3;
@@ -272,7 +288,7 @@ __device__ __forceinline__ GroupInfo group_info(const DecodeParams& p, const Cta
 
 // Issue ring stage i (global stage index within this CTA) into `slot`.
 template <int MT, bool HAS_ZP>
-__device__ __forceinline__ void issue_stage(const DecodeParams& p, const CtaPlan& q, const DecodeMaps& maps,
+__device__ __forceinline__ void issue_stage(const DecodeParams& p, const CtaPlan& q, const ProjMaps& maps,
                                             uint8_t* ring, uint64_t* full, int i, int slot) {
     using S = Shape<MT>;
     int g = (i < q.n4 * p.s_wide) ? i / p.s_wide : q.n4;
@@ -393,6 +409,8 @@ struct MathCtx {
     int slot;
     uint32_t phase;
     uint32_t epoch;         // fused all-gather: this call's epoch (0 on one GPU)
+    uint16_t* C;            // the CTA's projection: output and its columns
+    int N;
     bool aborted;
     int group;          // groups done (selects the reduction buffer)
 };
@@ -674,7 +692,7 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
     named_barrier(1, kMathThreads);
     const int col_base = kBoxCols * gi.tile0;
     int ncols = kBoxCols * gi.nt;
-    if (col_base + ncols > p.N) ncols = p.N - col_base;
+    if (col_base + ncols > x.N) ncols = x.N - col_base;
     for (int pair = x.warp; pair < nwc * M; pair += kWarps) {
         const int w = pair / M, m = pair - w * M;
         const int col = 32 * w + x.lane;
@@ -685,7 +703,7 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
             if (kSplitGroup)     // the second row half sits in columns 16..31 of each row block
                 for (int k = 0; k < rbs; ++k) v += red[(k * 32 + x.lane + kBoxCols) * rs + m];
             const uint16_t h = __half_as_ushort(__float2half_rn(v));
-            if (p.world == 1) p.C[(size_t)m * p.N + col_base + col] = h;
+            if (p.world == 1) x.C[(size_t)m * x.N + col_base + col] = h;
             hv = h;
         }
         if (p.world > 1) {
@@ -756,10 +774,11 @@ __device__ __forceinline__ void gather_complete(const DecodeParams& p) {
 }
 
 // One CTA per SM (its ring takes the SM's shared memory), so the register
-// budget is that of one CTA.
-template <int MT, bool SIGNED, bool HAS_ZP, bool FB8>
+// budget is that of one CTA.  NP: the projections a launch can hold (1, or
+// kMaxProj for a grouped launch); each CTA works on one of them.
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int NP>
 __global__ void __launch_bounds__(Shape<MT>::kThreads, 1)
-gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParams p) {
+gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps<NP> maps, const DecodeParams p) {
     using S = Shape<MT>;
     constexpr int kWarps = S::kWarps;
     extern __shared__ uint8_t smem_raw[];
@@ -775,7 +794,12 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     volatile int* sflag = reinterpret_cast<volatile int*>(prep_done + 1);   // [0] abort, [1] stages issued
 
     pdl_launch_dependents();
-    const CtaPlan q = cta_plan<MT>(p);
+    int j = 0;          // this CTA's projection
+#pragma unroll
+    for (int i = 1; i < NP; ++i)
+        if (i < p.nproj && (int)blockIdx.x >= p.proj_g0[i]) j = i;
+    const ProjMaps& pm = maps.proj[j];
+    const CtaPlan q = cta_plan(p, p.proj_T[j], p.proj_g0[j + 1] - p.proj_g0[j], blockIdx.x - (uint32_t)p.proj_g0[j]);
     const int tid = threadIdx.x;
     constexpr int kMathThreads = 32 * kWarps;
     if (tid == 0) {
@@ -793,20 +817,20 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     if (tid >= kMathThreads) {
         // ---------------- producer warp: every TMA copy of the ring
         if (tid == kMathThreads) {
-            prefetch_tmap(&maps.w_wide);
-            prefetch_tmap(&maps.w_narrow);
-            prefetch_tmap(&maps.s_wide);
-            prefetch_tmap(&maps.s_narrow);
-            prefetch_tmap(&maps.s_split);
+            prefetch_tmap(&pm.w_wide);
+            prefetch_tmap(&pm.w_narrow);
+            prefetch_tmap(&pm.s_wide);
+            prefetch_tmap(&pm.s_narrow);
+            prefetch_tmap(&pm.s_split);
             if constexpr (HAS_ZP) {
-                prefetch_tmap(&maps.z_wide);
-                prefetch_tmap(&maps.z_narrow);
-                prefetch_tmap(&maps.z_split);
+                prefetch_tmap(&pm.z_wide);
+                prefetch_tmap(&pm.z_narrow);
+                prefetch_tmap(&pm.z_split);
             }
             // weights, scales and zero points are never written by a kernel of
             // this library, so they may be fetched before the previous kernel ends
             const int early = q.total < p.early ? q.total : p.early;
-            for (int s = 0; s < early; ++s) issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, s, s);
+            for (int s = 0; s < early; ++s) issue_stage<MT, HAS_ZP>(p, q, pm, ring, full, s, s);
             sflag[1] = early;
             // The rest of the ring only once the activations are in: their
             // loads are on the critical path and should not queue behind this
@@ -818,7 +842,7 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
                     ok = false;
                 if (!ok || sflag[0]) break;
                 fence_proxy_async_smem();     // the math warps' reads of the slot before the copy overwrites it
-                issue_stage<MT, HAS_ZP>(p, q, maps, ring, full, i, slot);
+                issue_stage<MT, HAS_ZP>(p, q, pm, ring, full, i, slot);
                 sflag[1] = i + 1;
             }
             if (!ok) {
@@ -848,6 +872,8 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     x.slot = 0;
     x.phase = 0;
     x.epoch = 0;
+    x.C = p.proj_C[j];
+    x.N = p.proj_N[j];
     x.aborted = false;
     x.group = 0;
     GroupInfo gi = group_info(p, q, 0);
@@ -930,10 +956,9 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps maps, const DecodeParam
     if (p.world > 1 && p.barrier) gather_complete(p);
 }
 
-template <int MT, bool SIGNED, bool HAS_ZP, bool FB8>
-int launch(const DecodeMaps& maps, const DecodeParams& p, size_t smem,
-           cudaStream_t stream) {
-    auto kern = gemv_w4_decode_kernel<MT, SIGNED, HAS_ZP, FB8>;
+template <int MT, bool SIGNED, bool HAS_ZP, bool FB8, int NP>
+int launch(const DecodeMaps<NP>& maps, const DecodeParams& p, size_t smem, cudaStream_t stream) {
+    auto kern = gemv_w4_decode_kernel<MT, SIGNED, HAS_ZP, FB8, NP>;
     static SmemLimit limit;     // per instantiation, per device
     const int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem, &limit);
     if (st != T4B_OK) return st;
@@ -952,22 +977,23 @@ int launch(const DecodeMaps& maps, const DecodeParams& p, size_t smem,
     return T4B_OK;
 }
 
-template <int MT, bool SIGNED>
-int dispatch_zp(bool zp, bool fb8, const DecodeMaps& maps, const DecodeParams& p, size_t smem,
+template <int MT, bool SIGNED, int NP>
+int dispatch_zp(bool zp, bool fb8, const DecodeMaps<NP>& maps, const DecodeParams& p, size_t smem,
                 cudaStream_t stream) {
-    if (zp) return fb8 ? launch<MT, SIGNED, true, true>(maps, p, smem, stream)
-                       : launch<MT, SIGNED, true, false>(maps, p, smem, stream);
-    return fb8 ? launch<MT, SIGNED, false, true>(maps, p, smem, stream)
-               : launch<MT, SIGNED, false, false>(maps, p, smem, stream);
+    if (zp) return fb8 ? launch<MT, SIGNED, true, true, NP>(maps, p, smem, stream)
+                       : launch<MT, SIGNED, true, false, NP>(maps, p, smem, stream);
+    return fb8 ? launch<MT, SIGNED, false, true, NP>(maps, p, smem, stream)
+               : launch<MT, SIGNED, false, false, NP>(maps, p, smem, stream);
 }
 
-int dispatch(bool is_signed, bool zp, bool fb8, int MT, const DecodeMaps& maps, const DecodeParams& p, size_t smem,
-             cudaStream_t stream) {
+template <int NP>
+int dispatch(bool is_signed, bool zp, bool fb8, int MT, const DecodeMaps<NP>& maps, const DecodeParams& p,
+             size_t smem, cudaStream_t stream) {
     if (MT == 1)
-        return is_signed ? dispatch_zp<1, true>(zp, fb8, maps, p, smem, stream)
-                         : dispatch_zp<1, false>(zp, fb8, maps, p, smem, stream);
-    return is_signed ? dispatch_zp<2, true>(zp, fb8, maps, p, smem, stream)
-                     : dispatch_zp<2, false>(zp, fb8, maps, p, smem, stream);
+        return is_signed ? dispatch_zp<1, true, NP>(zp, fb8, maps, p, smem, stream)
+                         : dispatch_zp<1, false, NP>(zp, fb8, maps, p, smem, stream);
+    return is_signed ? dispatch_zp<2, true, NP>(zp, fb8, maps, p, smem, stream)
+                     : dispatch_zp<2, false, NP>(zp, fb8, maps, p, smem, stream);
 }
 
 // Dynamic shared memory one CTA may use on the current device (cached per device).
@@ -994,16 +1020,45 @@ int decode_device_error(cudaStream_t stream, unsigned* out, bool clear) {
     return e == cudaSuccess ? T4B_OK : record_cuda_error(e);
 }
 
-// plan_only: run every check and the shared-memory plan, launch nothing (the
-// pointers are not read; Z only says whether there are zero points).
-static int decode_impl(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M,
-                       int N, int K, int group, const T4BGather* gather, cudaStream_t stream,
-                       bool plan_only = false) {
+// Tensor maps of one projection (box shapes of the plan in p).
+static bool make_proj_maps(ProjMaps& m, const void* W, const void* S, const void* Z, int N, int K, int group,
+                           int rows_wide, int rows_narrow, const DecodeParams& p) {
+    const uint64_t KW = (uint64_t)(K / 8), G = (uint64_t)(K / group), n = (uint64_t)N;
+    if (!make_tmap_2d_ex(&m.w_wide, false, W, KW, n, rows_wide, kBoxCols, 64, 128) ||
+        !make_tmap_2d_ex(&m.w_narrow, false, W, KW, n, rows_narrow, kBoxCols, 64, 128) ||
+        !make_tmap_2d_ex(&m.s_wide, true, S, G, n, p.sbr_wide, 4 * kBoxCols, 0, 0) ||
+        !make_tmap_2d_ex(&m.s_narrow, true, S, G, n, p.sbr_narrow, 2 * kBoxCols, 0, 0) ||
+        !make_tmap_2d_ex(&m.s_split, true, S, G, n, p.sbr_split, kBoxCols, 0, 0))
+        return false;
+    if (Z) {
+        return make_tmap_2d_ex(&m.z_wide, true, Z, G, n, p.sbr_wide, 4 * kBoxCols, 0, 0) &&
+               make_tmap_2d_ex(&m.z_narrow, true, Z, G, n, p.sbr_narrow, 2 * kBoxCols, 0, 0) &&
+               make_tmap_2d_ex(&m.z_split, true, Z, G, n, p.sbr_split, kBoxCols, 0, 0);
+    }
+    m.z_wide = m.s_wide;       // never read
+    m.z_narrow = m.s_narrow;
+    m.z_split = m.s_split;
+    return true;
+}
+
+// The decode launch of np projections that read the same A (np = 1 for the
+// single ops and the fused gather).  Z is NULL (no zero points) or np
+// pointers, all set.  plan_only: run every check and the shared-memory plan,
+// launch nothing (no pointer is read; Z only says whether there are zero
+// points).  ctas, if given, receives each projection's CTA count.
+static int decode_impl(bool is_signed, const void* A, int np, const void* const* W, const void* const* S,
+                       const void* const* Z, void* const* C, const int* N, int M, int K, int group,
+                       const T4BGather* gather, cudaStream_t stream, bool plan_only = false, int* ctas = nullptr) {
+    if (np < 1 || np > kMaxProj || (gather && np != 1)) return T4B_ERR_UNSUPPORTED;
+    const bool has_zp = Z != nullptr;
     const int KW = K / 8;
     const int gw = group / 8;
     if (M > 16) return T4B_ERR_UNSUPPORTED;
-    if ((K % 128) != 0 || (N % 8) != 0) return T4B_ERR_UNSUPPORTED;
-    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(S, 16) || (Z && !aligned(Z, 16))) return T4B_ERR_UNSUPPORTED;
+    if ((K % 128) != 0 || !aligned(A, 16)) return T4B_ERR_UNSUPPORTED;
+    for (int j = 0; j < np; ++j) {
+        if ((N[j] % 8) != 0 || !aligned(W[j], 16) || !aligned(S[j], 16) || (has_zp && !aligned(Z[j], 16)))
+            return T4B_ERR_UNSUPPORTED;
+    }
     const int MT = (M <= 8) ? 1 : 2;
     const int warps = (MT == 1) ? Shape<1>::kWarps : Shape<2>::kWarps;
     const int rows_narrow = 16 * warps, rows_wide = 8 * warps, rows_split = 32 * warps;
@@ -1013,18 +1068,57 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
     if (!(gw == 8 || gw >= 16) || !box_rows(rows_wide) || !box_rows(rows_narrow)) return T4B_ERR_UNSUPPORTED;
     DecodeParams p;
     p.A = static_cast<const uint16_t*>(A);
-    p.C = static_cast<uint16_t*>(C);
-    p.M = M; p.N = N; p.K = K; p.KW = KW;
+    p.M = M; p.K = K; p.KW = KW;
     p.split = (box_rows(rows_split) && M <= 4) ? 1 : 0;         // split groups use 2 batch columns per row
     const int pad_rows = p.split ? rows_split : rows_narrow;       // a split stage may run past KW
     p.KWp = (KW + pad_rows - 1) / pad_rows * pad_rows;
-    p.T = (N + kBoxCols - 1) / kBoxCols;
-    p.G = p.T < sm_count() ? p.T : sm_count();
+    // Column tiles of each projection and the CTAs (at most one per SM) that
+    // share them: with more tiles than SMs, every projection gets a CTA and
+    // each further CTA goes to the projection with the most tiles per CTA
+    // (a CTA's stages are proportional to its tiles, K being common).
+    const int sms = sm_count();
+    int T[kMaxProj], G[kMaxProj];
+    long long t_total = 0;
+    for (int j = 0; j < np; ++j) {
+        T[j] = (N[j] + kBoxCols - 1) / kBoxCols;
+        t_total += T[j];
+    }
     // Every CTA stages all of A (M * K * 2 bytes).  Past M * K = 32768 that
     // only pays when each SM has at least one whole column tile to spend it
     // on; narrower shapes go to the K-split stream kernel.
-    if ((long long)M * K > 32768 && p.T < sm_count()) return T4B_ERR_UNSUPPORTED;
-    if ((long long)p.T * p.G >= (1ll << 32)) return T4B_ERR_UNSUPPORTED;
+    if ((long long)M * K > 32768 && t_total < sms) return T4B_ERR_UNSUPPORTED;
+    int used = 0;
+    if (t_total <= sms) {
+        for (int j = 0; j < np; ++j) G[j] = T[j];
+        used = (int)t_total;
+    } else {
+        if (np > sms) return T4B_ERR_UNSUPPORTED;
+        for (int j = 0; j < np; ++j) G[j] = 1;
+        used = np;
+        while (used < sms) {
+            int best = -1;
+            for (int j = 0; j < np; ++j)
+                if (G[j] < T[j] && (best < 0 || (long long)T[j] * G[best] > (long long)T[best] * G[j])) best = j;
+            if (best < 0) break;
+            ++G[best];
+            ++used;
+        }
+    }
+    for (int j = 0; j < np; ++j)
+        if ((long long)T[j] * G[j] >= (1ll << 32)) return T4B_ERR_UNSUPPORTED;
+    p.nproj = np;
+    p.proj_g0[0] = 0;
+    for (int j = 0; j < kMaxProj; ++j) {
+        const bool in = j < np;
+        p.proj_g0[j + 1] = p.proj_g0[j] + (in ? G[j] : 0);
+        p.proj_T[j] = in ? T[j] : 0;
+        p.proj_N[j] = in ? N[j] : 0;
+        p.proj_C[j] = (in && C) ? static_cast<uint16_t*>(C[j]) : nullptr;
+    }
+    p.T = (int)t_total;
+    p.G = used;
+    p.N = N[0];
+    p.C = p.proj_C[0];
     p.gw = gw;
     p.gw_shift = -1;
     if ((gw & (gw - 1)) == 0) {
@@ -1046,7 +1140,7 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
     p.kwdiv = make_fastdiv((uint32_t)p.KWp);
     p.world = 1;
     p.rank = 0;
-    p.n_total = N;
+    p.n_total = N[0];
     p.col_offset = 0;
     p.barrier = 0;
     p.gout = nullptr;
@@ -1063,13 +1157,15 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
         for (int g = 0; g < p.world; ++g) p.recv[g] = static_cast<unsigned long long*>(gather->recv[g]);
     }
     const int weight_bytes = warps * 2048;
-    p.slot_bytes = (weight_bytes + p.s_bytes * (Z ? 2 : 1) + 1023) / 1024 * 1024;
+    p.slot_bytes = (weight_bytes + p.s_bytes * (has_zp ? 2 : 1) + 1023) / 1024 * 1024;
     const size_t fixed = 1024 + (size_t)p.act_bytes + 4 * (size_t)(p.sum_floats + p.red_floats) + kMaxStages * 16 + 8 + 16;
     // one CTA per SM with the deepest ring shared memory allows
     const size_t budget = smem_budget();
     int stages = fixed < budget ? (int)((budget - fixed) / p.slot_bytes) : 0;
     if (stages > kMaxStages) stages = kMaxStages;
     if (stages < 2) return T4B_ERR_UNSUPPORTED;
+    if (ctas)
+        for (int j = 0; j < np; ++j) ctas[j] = G[j];
     if (plan_only) return T4B_OK;
     p.stages = stages;
     // Every stage the ring holds is fetched before the previous kernel ends:
@@ -1079,35 +1175,48 @@ static int decode_impl(bool is_signed, const void* A, const void* W, const void*
     p.early = stages;
     const size_t smem = fixed + (size_t)stages * p.slot_bytes;
 
-    DecodeMaps maps;
-    if (!make_tmap_2d_ex(&maps.w_wide, false, W, (uint64_t)KW, (uint64_t)N, rows_wide, kBoxCols, 64, 128) ||
-        !make_tmap_2d_ex(&maps.w_narrow, false, W, (uint64_t)KW, (uint64_t)N, rows_narrow, kBoxCols, 64, 128) ||
-        !make_tmap_2d_ex(&maps.s_wide, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_wide, 4 * kBoxCols, 0, 0) ||
-        !make_tmap_2d_ex(&maps.s_narrow, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_narrow, 2 * kBoxCols, 0, 0) ||
-        !make_tmap_2d_ex(&maps.s_split, true, S, (uint64_t)(K / group), (uint64_t)N, p.sbr_split, kBoxCols, 0, 0))
-        return T4B_ERR_UNSUPPORTED;
-    if (Z) {
-        if (!make_tmap_2d_ex(&maps.z_wide, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_wide, 4 * kBoxCols, 0, 0) ||
-            !make_tmap_2d_ex(&maps.z_narrow, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_narrow, 2 * kBoxCols, 0, 0) ||
-            !make_tmap_2d_ex(&maps.z_split, true, Z, (uint64_t)(K / group), (uint64_t)N, p.sbr_split, kBoxCols, 0, 0))
+    if (np == 1) {
+        DecodeMaps<1> maps;
+        if (!make_proj_maps(maps.proj[0], W[0], S[0], has_zp ? Z[0] : nullptr, N[0], K, group, rows_wide, rows_narrow, p))
             return T4B_ERR_UNSUPPORTED;
-    } else {
-        maps.z_wide = maps.s_wide;       // never read
-        maps.z_narrow = maps.s_narrow;
-        maps.z_split = maps.s_split;
+        return dispatch<1>(is_signed, has_zp, p.fb == 8, MT, maps, p, smem, stream);
     }
-    return dispatch(is_signed, Z != nullptr, p.fb == 8, MT, maps, p, smem, stream);
+    DecodeMaps<kMaxProj> maps;
+    for (int j = 0; j < np; ++j)
+        if (!make_proj_maps(maps.proj[j], W[j], S[j], has_zp ? Z[j] : nullptr, N[j], K, group, rows_wide, rows_narrow,
+                            p))
+            return T4B_ERR_UNSUPPORTED;
+    for (int j = np; j < kMaxProj; ++j) maps.proj[j] = maps.proj[0];     // never read
+    return dispatch<kMaxProj>(is_signed, has_zp, p.fb == 8, MT, maps, p, smem, stream);
 }
 
 int gemv_w4_decode(bool is_signed, const void* A, const void* W, const void* S, const void* Z, void* C, int M, int N,
                    int K, int group, cudaStream_t stream) {
-    return decode_impl(is_signed, A, W, S, Z, C, M, N, K, group, nullptr, stream);
+    void* Cs[1] = {C};
+    return decode_impl(is_signed, A, 1, &W, &S, Z ? &Z : nullptr, Cs, &N, M, K, group, nullptr, stream);
 }
 
 int gemv_w4_decode_supported(int M, int N, int K, int group, bool has_zero_points) {
     // a stand-in zero-point pointer: only its presence matters to the plan
-    const void* z = has_zero_points ? reinterpret_cast<const void*>(uintptr_t{256}) : nullptr;
-    return decode_impl(true, nullptr, nullptr, nullptr, z, nullptr, M, N, K, group, nullptr, nullptr, true);
+    const void* z = reinterpret_cast<const void*>(uintptr_t{256});
+    const void* none = nullptr;
+    return decode_impl(true, nullptr, 1, &none, &none, has_zero_points ? &z : nullptr, nullptr, &N, M, K, group,
+                       nullptr, nullptr, true);
+}
+
+int gemv_w4_decode_grouped(bool is_signed, const void* A, int np, const void* const* W, const void* const* S,
+                           const void* const* Z, void* const* C, const int* N, int M, int K, int group,
+                           cudaStream_t stream) {
+    return decode_impl(is_signed, A, np, W, S, Z, C, N, M, K, group, nullptr, stream);
+}
+
+int gemv_w4_decode_grouped_plan(int np, const int* N, int M, int K, int group, bool has_zero_points, int* ctas) {
+    if (np < 1 || np > kMaxProj) return T4B_ERR_UNSUPPORTED;
+    const void* none[kMaxProj] = {};
+    const void* z[kMaxProj];
+    for (int j = 0; j < kMaxProj; ++j) z[j] = reinterpret_cast<const void*>(uintptr_t{256});
+    return decode_impl(true, nullptr, np, none, none, has_zero_points ? z : nullptr, nullptr, N, M, K, group, nullptr,
+                       nullptr, true, ctas);
 }
 
 int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const void* S, const void* Z, int M, int N,
@@ -1122,7 +1231,7 @@ int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const vo
         if (!g->recv[r]) return T4B_ERR_NULL_POINTER;
         if (reinterpret_cast<uintptr_t>(g->recv[r]) & 7) return T4B_ERR_MISALIGNED;
     }
-    return decode_impl(is_signed, A, W, S, Z, nullptr, M, N, K, group, g, stream);
+    return decode_impl(is_signed, A, 1, &W, &S, Z ? &Z : nullptr, nullptr, &N, M, K, group, g, stream);
 }
 
 }  // namespace t4b

@@ -18,13 +18,16 @@ Extensions, all backward compatible (trailing keyword arguments):
     hard-codes 100).
 """
 
+import ctypes
+
 import torch
 
 from . import _lib
 
 __all__ = [
     "dequantize_u4", "dequantize_s4", "dequantize_s3", "dequantize_fp8",
-    "fused_w4a16_gemm_u4", "fused_w4a16_gemm_s4", "fused_h17_gemv_s3", "fused_w8a16_gemm_fp8",
+    "fused_w4a16_gemm_u4", "fused_w4a16_gemm_s4", "fused_w4a16_gemm_grouped", "fused_h17_gemv_s3",
+    "fused_w8a16_gemm_fp8",
     "set_gemv_kernel", "device_error",
 ]
 
@@ -221,12 +224,15 @@ def _fail(msg):
     raise RuntimeError(msg)
 
 
-def _fused(name, A, W_packed, scales, zero_points):
-    # The decode path calls this once per projection per token, so the host
-    # work is kept short: the same checks as bindings.cpp:64-132 in the same
-    # order, with messages formatted only on failure.
+def _check_a(A):
     if not A.is_cuda:
         _fail("A must be a CUDA tensor")
+
+
+def _check_w(A, W_packed, scales, zero_points):
+    """The checks of bindings.cpp:64-132 after A's device check, in the same
+    order, with messages formatted only on failure; returns (M, N, K, G,
+    has_zp)."""
     if not W_packed.is_cuda:
         _fail("W_packed must be a CUDA tensor")
     if not scales.is_cuda:
@@ -261,10 +267,23 @@ def _fused(name, A, W_packed, scales, zero_points):
     G = _group_rows(scales, N, K, "scales")
     if has_zp and _group_rows(zero_points, N, K, "zero_points") != G:
         _fail("zero_points must have the same shape as scales")
+    return M, N, K, G, has_zp
+
+
+def _contig(t):
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _fused(name, A, W_packed, scales, zero_points):
+    # The decode path calls this once per projection per token, so the host
+    # work is kept short.
+    _check_a(A)
+    M, N, K, G, has_zp = _check_w(A, W_packed, scales, zero_points)
     A_ = _aligned16(A)
-    W_ = W_packed if W_packed.is_contiguous() else W_packed.contiguous()
-    S_ = scales if scales.is_contiguous() else scales.contiguous()
-    Z_ = (zero_points if zero_points.is_contiguous() else zero_points.contiguous()) if has_zp else None
+    W_ = _contig(W_packed)
+    S_ = _contig(scales)
+    Z_ = _contig(zero_points) if has_zp else None
+    dev = A.device
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
     cur = torch.cuda.current_device()
     idx = dev.index if dev.index is not None else cur
@@ -279,6 +298,50 @@ def _fused(name, A, W_packed, scales, zero_points):
     if st:
         _lib.check(st, name)
     return C
+
+
+def _fused_grouped(A, W_list, scales_list, zero_points_list, signed):
+    n = len(W_list)
+    if n < 1 or n > GROUPED_MAX:
+        _fail(f"a grouped call takes 1 to {GROUPED_MAX} projections, got {n}")
+    if len(scales_list) != n or (zero_points_list is not None and len(zero_points_list) != n):
+        _fail("W_packed, scales and zero_points lists must have the same length")
+    _check_a(A)
+    shapes, zs = [], []
+    for j in range(n):
+        z = zero_points_list[j] if zero_points_list is not None else None
+        M, N, K, G, has_zp = _check_w(A, W_list[j], scales_list[j], z)
+        shapes.append((N, G))
+        zs.append(z if has_zp else None)
+    if len({G for _, G in shapes}) != 1:
+        _fail("every projection of a grouped call must have the same group size")
+    has_zp = zs[0] is not None
+    if any((z is not None) != has_zp for z in zs):
+        _fail("zero_points must be given for every projection of a grouped call or for none")
+    G = shapes[0][1]
+    A_ = _aligned16(A)
+    Ws = [_contig(w) for w in W_list]
+    Ss = [_contig(t) for t in scales_list]
+    Zs = [_contig(z) for z in zs] if has_zp else None
+    dev = A.device
+    Cs = [torch.empty((M, N), dtype=torch.float16, device=dev) for N, _ in shapes]
+    vp = ctypes.c_void_p * n
+    cur = torch.cuda.current_device()
+    idx = dev.index if dev.index is not None else cur
+    if cur != idx:
+        torch.cuda.set_device(idx)
+    try:
+        st = _entry("t4b_fused_w4a16_gemm_grouped")(
+            A_.data_ptr(), n, vp(*[w.data_ptr() for w in Ws]), vp(*[t.data_ptr() for t in Ss]),
+            vp(*[z.data_ptr() for z in Zs]) if Zs is not None else None, vp(*[c.data_ptr() for c in Cs]),
+            (ctypes.c_int * n)(*[N for N, _ in shapes]), M, K, K // G, 1 if signed else 0,
+            torch._C._cuda_getCurrentRawStream(idx))
+    finally:
+        if cur != idx:
+            torch.cuda.set_device(cur)
+    if st:
+        _lib.check(st, "t4b_fused_w4a16_gemm_grouped")
+    return Cs
 
 
 _BIND = False      # the torch binding module once looked up (None: not built)
@@ -300,7 +363,8 @@ def _binding():
             lib = _lib.load()
             addr = lambda f: ctypes.cast(f, ctypes.c_void_p).value    # noqa: E731
             b.init(addr(lib.t4b_fused_w4a16_gemm_u4), addr(lib.t4b_fused_w4a16_gemm_s4),
-                   addr(lib.t4b_fused_w4a16_gemv_allgather), addr(lib.t4b_status_string),
+                   addr(lib.t4b_fused_w4a16_gemv_allgather), addr(lib.t4b_fused_w4a16_gemm_grouped),
+                   addr(lib.t4b_status_string),
                    addr(lib.t4b_last_cuda_error), _lib.T4BError)
         _BIND = b
     return _BIND
@@ -320,6 +384,42 @@ def fused_w4a16_gemm_s4(A, W_packed, scales, zero_points):
     if b is not None:
         return b.fused_w4a16_gemm_s4(A, W_packed, scales, zero_points)
     return _fused("t4b_fused_w4a16_gemm_s4", A, W_packed, scales, zero_points)
+
+
+GROUPED_MAX = 4      # T4B_GROUPED_MAX
+
+
+def grouped_plan(N_list, M, K, group_size, has_zero_points=False):
+    """CTAs per projection of the one decode launch that
+    ``fused_w4a16_gemm_grouped`` makes for these shapes on the current
+    device, or None when it makes one launch per projection instead."""
+    n = len(N_list)
+    ctas = (ctypes.c_int * max(n, 1))()
+    st = _lib.load().t4b_fused_w4a16_gemm_grouped_plan(n, (ctypes.c_int * max(n, 1))(*N_list), M, K, group_size,
+                                                        1 if has_zero_points else 0, ctas)
+    if st == 4:         # T4B_ERR_UNSUPPORTED
+        return None
+    _lib.check(st, "t4b_fused_w4a16_gemm_grouped_plan")
+    return list(ctas[:n])
+
+
+def fused_w4a16_gemm_grouped(A, W_list, scales_list, zero_points_list=None, signed=True):
+    """Projections that read the same activation, in one call:
+    ``[A @ dequant(W) for W in W_list]`` (s4 weights if ``signed``, else u4),
+    each with its scales and zero points (``zero_points_list`` None, or one
+    tensor per projection; all given or all None/empty), the same K and group
+    size.  No counterpart in the reference, whose op takes one projection (a
+    layer's q/k/v or gate/up are separate ``fused_w4a16_gemm_{s4,u4}`` calls);
+    the results match those calls within the ops' tolerance.  For M <= 16 the
+    projections run as one decode launch whose CTAs are shared out by column
+    tiles; otherwise as one launch per projection.  Each projection is
+    checked as ``fused_w4a16_gemm_{s4,u4}`` checks it."""
+    b = _BIND if _BIND is not False else _binding()
+    if b is not None:
+        return b.fused_w4a16_gemm_grouped(A, list(W_list), list(scales_list),
+                                          None if zero_points_list is None else list(zero_points_list),
+                                          bool(signed))
+    return _fused_grouped(A, W_list, scales_list, zero_points_list, signed)
 
 
 # ------------------------------------------------------- FP8-E4M3 weight GEMM

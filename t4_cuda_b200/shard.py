@@ -86,6 +86,7 @@ class ShardedGroup:
         self.pg = process_group
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self._graph = None
+        self._grouped = _grouped_args(self.linears)
 
     def capture_local(self, x):
         """Record this rank's local projections of activation ``x`` and their
@@ -106,8 +107,17 @@ class ShardedGroup:
     def release_graph(self):
         self._graph = self._x = self._packed = None
 
+    def _local_list(self, x):
+        """This rank's outputs of every projection: one grouped call
+        (ops.fused_w4a16_gemm_grouped) where the group allows it, else one
+        call per projection (and for CPU tensors, which the ops reject as
+        each projection's call does)."""
+        if self._grouped is not None and x.is_cuda:
+            return ops.fused_w4a16_gemm_grouped(x, *self._grouped)
+        return [lin.local(x) for lin in self.linears]
+
     def _local_packed(self, x):
-        locals_ = [lin.local(x) for lin in self.linears]
+        locals_ = self._local_list(x)
         widths = [t.size(1) for t in locals_]
         packed = torch.cat(locals_, dim=1) if len(locals_) > 1 else locals_[0]
         return packed, widths
@@ -118,7 +128,7 @@ class ShardedGroup:
             packed, widths = self._packed, self._widths
         else:
             if self.world == 1:
-                return [lin.local(x) for lin in self.linears]
+                return self._local_list(x)
             packed, widths = self._local_packed(x)
         if self.world == 1:
             return [t.clone() for t in _split_columns(packed, widths)]
@@ -128,6 +138,27 @@ class ShardedGroup:
         gathered = torch.empty((self.world * M, packed.size(1)), dtype=packed.dtype, device=packed.device)
         dist.all_gather_into_tensor(gathered, packed.contiguous(), group=self.pg)
         return unpack_gathered(gathered.view(self.world, M, packed.size(1)), widths)
+
+
+def _grouped_args(linears):
+    """(W list, scales list, zero points list or None, signed) for one
+    grouped call of these projections, or None when they do not form one:
+    fewer than two, more than ops.GROUPED_MAX, not all s4 or all u4, or with
+    different K, group sizes or presence of zero points."""
+    if not 2 <= len(linears) <= ops.GROUPED_MAX:
+        return None
+    fmts = {lin.fmt for lin in linears}
+    if fmts not in ({"s4"}, {"u4"}):
+        return None
+    def group_rows(t):
+        return t.size(0) if t.dim() == 2 else 1
+    if len({lin.W.size(0) for lin in linears}) != 1 or len({group_rows(lin.S) for lin in linears}) != 1:
+        return None
+    has_zp = [lin.Z is not None and lin.Z.numel() > 0 for lin in linears]
+    if any(h != has_zp[0] for h in has_zp):
+        return None
+    Zs = [lin.Z for lin in linears] if has_zp[0] else None
+    return [lin.W for lin in linears], [lin.S for lin in linears], Zs, fmts == {"s4"}
 
 
 def _split_columns(packed, widths):

@@ -89,3 +89,28 @@ def test_noalloc_gemv_argument_validation(lib):
     assert f(_fake(0x10008), p, p, None, p, 1, 64, 64, 64, 0, None) == 3   # A must be 16-byte aligned
     assert f(p, p, p, None, p, 17, 64, 64, 64, 1, None) == 4      # M > 16 is not a decode shape
     assert f(p, p, p, None, p, 1, 62, 64, 64, 1, None) == 4       # N % 4
+
+
+def test_grouped_gemm_argument_validation(lib):
+    p = _fake()
+    vp2 = ctypes.c_void_p * 2
+    ptrs = vp2(0x10000, 0x20000)
+    Ns = (ctypes.c_int * 2)(64, 64)
+    f = lib.t4b_fused_w4a16_gemm_grouped
+    assert f(p, 0, ptrs, ptrs, None, ptrs, Ns, 1, 64, 64, 1, None) == 1        # no projection
+    assert f(p, 5, ptrs, ptrs, None, ptrs, Ns, 1, 64, 64, 1, None) == 1        # more than T4B_GROUPED_MAX
+    assert f(p, 2, ptrs, ptrs, None, ptrs, Ns, 0, 64, 64, 1, None) == 1        # M = 0
+    assert f(p, 2, ptrs, ptrs, None, ptrs, Ns, 1, 64, 48, 1, None) == 1        # group does not divide K
+    assert f(p, 2, ptrs, ptrs, None, ptrs, (ctypes.c_int * 2)(64, 0), 1, 64, 64, 1, None) == 1   # N = 0
+    assert f(None, 2, ptrs, ptrs, None, ptrs, Ns, 1, 64, 64, 1, None) == 2     # null A
+    assert f(p, 2, None, ptrs, None, ptrs, Ns, 1, 64, 64, 1, None) == 2        # null weight list
+    assert f(p, 2, vp2(0x10000, None), ptrs, None, ptrs, Ns, 1, 64, 64, 1, None) == 2   # null weight
+    assert f(p, 2, ptrs, ptrs, vp2(0x10000, None), ptrs, Ns, 1, 64, 64, 1, None) == 2   # zero points: all or none
+    assert f(_fake(0x10008), 2, ptrs, ptrs, None, ptrs, Ns, 1, 64, 64, 1, None) == 3   # A 16-byte aligned
+    assert f(p, 2, vp2(0x10000, 0x20002), ptrs, None, ptrs, Ns, 1, 64, 64, 1, None) == 3   # W 4-byte aligned
+    plan = lib.t4b_fused_w4a16_gemm_grouped_plan
+    ctas = (ctypes.c_int * 2)()
+    assert plan(0, Ns, 1, 64, 64, 0, ctas) == 1
+    assert plan(2, Ns, 1, 60, 60, 0, ctas) == 1                                 # K % 8
+    assert plan(2, None, 1, 64, 64, 0, ctas) == 2
+    assert plan(2, Ns, 17, 64, 64, 0, ctas) == 4                                # M > 16: one launch each

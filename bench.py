@@ -679,6 +679,29 @@ def run_ours(args):
             us = e0.elapsed_time(e1) * 1e3 / (reps * len(layers))
             per_shape[f"{name}_{K}x{N}"] = {"us": round(us, 3), "GB/s": round(alg_bytes(M, K, N) / us / 1e3, 1)}
             del g
+        # the grouped launches of the step: one call per group, a graph over the pool
+        for a_name, names in GATHERS:
+            grp0 = pg_layers[0][GATHERS.index((a_name, names))]
+            if len(names) < 2 or getattr(grp0, "_grouped", None) is None:
+                continue
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for li in range(pool):
+                    pg_layers[li][GATHERS.index((a_name, names))](acts[a_name])
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 20
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * pool)
+            byts = sum(alg_bytes(M, K, N) for n, K, N in PROJ if n in names)
+            per_shape["+".join(names) + "_grouped"] = {"us": round(us, 3), "GB/s": round(byts / us / 1e3, 1)}
+            del g
 
     # ---- second half of the metric: prefill GEMM at M = 4096 (one GPU)
     gemm = None
@@ -931,7 +954,8 @@ def run_case(spec, launches=6):
       gemm:M:K:N     s4 group-128 prefill GEMM (tcgen05)
       int3:K:N       H17 INT3 GEMV, M = 1, group 128 (K a multiple of 10)
       int3gemm:M:K:N H17 INT3 prefill GEMM (tcgen05), group 128
-      dequant:KIND:W flat dequant (KIND s4, s3 or fp8; magic mode) of W words"""
+      dequant:KIND:W flat dequant (KIND s4, s3 or fp8; magic mode) of W words
+      grouped:K:N1+N2+..:M  one grouped decode call of projections N1, N2, .."""
     from t4_cuda_b200 import ops
     kind, *dims = spec.split(":")
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
@@ -966,6 +990,15 @@ def run_case(spec, launches=6):
         Z = torch.empty(0, dtype=torch.float16, device=dev)
         for _ in range(launches):
             C = ops.fused_h17_gemv_s3(A, W, S, Z, group_size=128)
+    elif kind == "grouped":
+        K, Ns, M = int(dims[0]), [int(x) for x in dims[1].split("+")], int(dims[2])
+        sets = pool_of(sum(K * N // 2 for N in Ns), lambda: [
+            torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=gen)
+            for N in Ns])
+        Ss = [(torch.randn((K // GROUP, N), device=dev, generator=gen).abs() * 0.02 + 1e-3).half() for N in Ns]
+        A = torch.randn((M, K), device=dev, generator=gen).half()
+        for i in range(launches):
+            C = ops.fused_w4a16_gemm_grouped(A, sets[i % len(sets)], Ss)[0]
     elif kind == "dequant":
         dk, words = dims[0], int(dims[1])
         per = {"s4": 8, "s3": 10, "fp8": 4}[dk]

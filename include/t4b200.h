@@ -233,6 +233,22 @@ int t4b_fused_w4a16_gemv_allgather(const void* A, const void* W_packed, const vo
                                    const void* zero_points, int M, int N, int K, int group_size,
                                    int is_signed, const T4BGather* gather, void* stream);
 
+/* The n projections of a group (1 <= n <= T4B_GROUPED_MAX, same K, group_size,
+ * signedness and presence of zero points) as one launch of the decode kernel
+ * with the fused all-gather: projection j stores its N[j] columns at columns
+ * [col_offsets[j], col_offsets[j] + N[j]) of the group buffer (even offsets
+ * and widths); gather->col_offset is not used, gather->barrier as above (1
+ * when this call is the group's last).  No counterpart in the reference.
+ * Returns T4B_ERR_UNSUPPORTED (nothing launched) where the decode kernel does
+ * not take the shapes as one launch (t4b_fused_w4a16_gemm_grouped_plan says
+ * which); the caller then makes one t4b_fused_w4a16_gemv_allgather call per
+ * projection. */
+int t4b_fused_w4a16_gemv_allgather_grouped(const void* A, int n, const void* const* W_packed,
+                                           const void* const* scales, const void* const* zero_points,
+                                           const int* N, const int* col_offsets, int M, int K,
+                                           int group_size, int is_signed, const T4BGather* gather,
+                                           void* stream);
+
 /* Device memory another process on this node can map: cudaMalloc'd and zeroed
  * (t4b_ipc_alloc), its 64-byte handle (t4b_ipc_handle), the peer's mapping of
  * a handle (t4b_ipc_open) and their release. */

@@ -29,6 +29,8 @@ SIGNATURES = {
     "t4b_fused_w4a16_gemv_noalloc": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp],
     "t4b_fused_w4a16_gemv_allgather": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp],
     "t4b_fused_w4a16_gemv_allgather_supported": [_i32, _i32, _i32, _i32, _i32],
+    "t4b_fused_w4a16_gemv_allgather_grouped": [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp,
+                                               _vp],
     "t4b_ipc_alloc": [ctypes.c_size_t, ctypes.POINTER(_vp)],
     "t4b_ipc_free": [_vp],
     "t4b_ipc_handle": [_vp, _vp],

@@ -25,6 +25,10 @@ using FusedFn = int (*)(const void*, const void*, const void*, const void*, void
 // t4b_fused_w4a16_gemv_allgather(A, W, S, Z, M, N, K, group, is_signed, gather, stream)
 using AllgatherFn = int (*)(const void*, const void*, const void*, const void*, int, int, int, int, int, const void*,
                             void*);
+// t4b_fused_w4a16_gemv_allgather_grouped(A, n, W[], S[], Z[], N[], col_offsets[], M, K, group, is_signed,
+//                                        gather, stream)
+using AllgatherGroupedFn = int (*)(const void*, int, const void* const*, const void* const*, const void* const*,
+                                   const int*, const int*, int, int, int, int, const void*, void*);
 // t4b_fused_w4a16_gemm_grouped(A, n, W[], S[], Z[], C[], N[], M, K, group, is_signed, stream)
 using GroupedFn = int (*)(const void*, int, const void* const*, const void* const*, const void* const*, void* const*,
                           const int*, int, int, int, int, void*);
@@ -34,6 +38,7 @@ using LastCudaErrorFn = int (*)();
 FusedFn g_u4 = nullptr, g_s4 = nullptr;
 AllgatherFn g_allgather = nullptr;
 GroupedFn g_grouped = nullptr;
+AllgatherGroupedFn g_allgather_grouped = nullptr;
 StatusStringFn g_status_string = nullptr;
 LastCudaErrorFn g_last_cuda_error = nullptr;
 PyObject* g_error_class = nullptr;      // t4_cuda_b200._lib.T4BError (a RuntimeError)
@@ -225,18 +230,49 @@ void allgather_group(const torch::Tensor& x, const torch::Tensor& table, int64_t
     }
 }
 
+// One call of a fused-gather group made as one grouped launch
+// (shard.P2PGatherGroup with grouped=True): int64 table [n, 9] -- W, scales,
+// zero points (0: none), N, K, group size, is_signed, address of the group's
+// T4BGather, the projection's first column in the group buffer.
+void allgather_grouped(const torch::Tensor& x, const torch::Tensor& table, int64_t M) {
+    if (!g_allgather_grouped) fail("t4_cuda_b200 torch binding not initialised");
+    if (!x.is_cuda() || x.scalar_type() != torch::kFloat16 || !x.is_contiguous() || x.dim() != 2 || x.size(0) != M)
+        fail("the fused gather group takes contiguous fp16 activations of " + std::to_string(M) + " rows");
+    const int64_t n = table.size(0);
+    if (table.is_cuda() || table.scalar_type() != torch::kInt64 || table.dim() != 2 || table.size(1) != 9 ||
+        !table.is_contiguous() || n < 1 || n > kGroupedMax)
+        fail("grouped gather table must be a contiguous CPU int64 [n, 9] tensor, 1 <= n <= 4");
+    const int64_t* t = table.data_ptr<int64_t>();
+    const void *wp[kGroupedMax], *sp[kGroupedMax], *zp[kGroupedMax];
+    int Ns[kGroupedMax], offs[kGroupedMax];
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t* r = t + 9 * i;
+        wp[i] = reinterpret_cast<const void*>(r[0]);
+        sp[i] = reinterpret_cast<const void*>(r[1]);
+        zp[i] = reinterpret_cast<const void*>(r[2]);
+        Ns[i] = (int)r[3];
+        offs[i] = (int)r[8];
+    }
+    const c10::cuda::CUDAGuard guard(x.device());
+    void* stream = c10::cuda::getCurrentCUDAStream(x.device().index()).stream();
+    const int st = g_allgather_grouped(x.data_ptr(), (int)n, wp, sp, t[2] ? zp : nullptr, Ns, offs, (int)M, (int)t[4],
+                                       (int)t[5], (int)t[6], reinterpret_cast<const void*>(t[7]), stream);
+    if (st) raise_status(st, "t4b_fused_w4a16_gemv_allgather_grouped");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "torch binding of t4_cuda_b200's fused W4A16 ops and fused-gather group calls (the hot paths)";
     m.def(
         "init",
-        [](uintptr_t u4, uintptr_t s4, uintptr_t allgather, uintptr_t grouped, uintptr_t status_string,
-           uintptr_t last_cuda_error, pybind11::object error_class) {
+        [](uintptr_t u4, uintptr_t s4, uintptr_t allgather, uintptr_t grouped, uintptr_t allgather_grouped,
+           uintptr_t status_string, uintptr_t last_cuda_error, pybind11::object error_class) {
             g_u4 = reinterpret_cast<FusedFn>(u4);
             g_s4 = reinterpret_cast<FusedFn>(s4);
             g_allgather = reinterpret_cast<AllgatherFn>(allgather);
             g_grouped = reinterpret_cast<GroupedFn>(grouped);
+            g_allgather_grouped = reinterpret_cast<AllgatherGroupedFn>(allgather_grouped);
             g_status_string = reinterpret_cast<StatusStringFn>(status_string);
             g_last_cuda_error = reinterpret_cast<LastCudaErrorFn>(last_cuda_error);
             Py_XDECREF(g_error_class);
@@ -252,6 +288,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "[A @ dequant(W) for W in W_list]: projections that read the same activation, in one call",
           pybind11::arg("A"), pybind11::arg("W_list"), pybind11::arg("scales_list"),
           pybind11::arg("zero_points_list"), pybind11::arg("is_signed"));
+    m.def("allgather_grouped", &allgather_grouped, "One fused-gather group call as one grouped launch, from its table",
+          pybind11::arg("x"), pybind11::arg("table"), pybind11::arg("M"));
     m.def("allgather_group", &allgather_group, "The launches of one fused-gather group call, from its table",
           pybind11::arg("x"), pybind11::arg("table"), pybind11::arg("M"));
 }

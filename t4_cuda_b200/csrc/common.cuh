@@ -63,6 +63,11 @@ int gemv_w4_decode_grouped(bool is_signed, const void* A, int np, const void* co
                            cudaStream_t stream);
 // The CTAs of each projection of that launch (nothing is launched).
 int gemv_w4_decode_grouped_plan(int np, const int* N, int M, int K, int group, bool has_zero_points, int* ctas);
+// The same launch with the fused all-gather: projection j's columns go to
+// [col_offsets[j], col_offsets[j] + N[j]) of the group buffer of g.
+int gemv_w4_decode_gather_grouped(bool is_signed, const void* A, int np, const void* const* W, const void* const* S,
+                                  const void* const* Z, const int* N, const int* col_offsets, int M, int K, int group,
+                                  const T4BGather* g, cudaStream_t stream);
 
 // Reads (and optionally clears) the decode GEMV's device error word on the
 // current device; synchronizes `stream`.

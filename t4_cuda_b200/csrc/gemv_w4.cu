@@ -402,6 +402,21 @@ int t4b_fused_w4a16_gemv_allgather_supported(int M, int N, int K, int group_size
     return t4b::gemv_w4_decode_supported(M, N, K, group_size, has_zero_points != 0);
 }
 
+int t4b_fused_w4a16_gemv_allgather_grouped(const void* A, int n, const void* const* W_packed,
+                                           const void* const* scales, const void* const* zero_points, const int* N,
+                                           const int* col_offsets, int M, int K, int group_size, int is_signed,
+                                           const T4BGather* gather, void* stream) {
+    if (n < 1 || n > T4B_GROUPED_MAX || M < 1 || K < 8 || (K % 8) != 0) return T4B_ERR_INVALID_VALUE;
+    if (group_size < 8 || (group_size % 8) != 0 || (K % group_size) != 0) return T4B_ERR_INVALID_VALUE;
+    if (!A || !W_packed || !scales || !N || !col_offsets || !gather) return T4B_ERR_NULL_POINTER;
+    for (int j = 0; j < n; ++j) {
+        if (N[j] < 1) return T4B_ERR_INVALID_VALUE;
+        if (!W_packed[j] || !scales[j] || (zero_points && !zero_points[j])) return T4B_ERR_NULL_POINTER;
+    }
+    return t4b::gemv_w4_decode_gather_grouped(is_signed != 0, A, n, W_packed, scales, zero_points, N, col_offsets, M,
+                                              K, group_size, gather, static_cast<cudaStream_t>(stream));
+}
+
 int t4b_fused_w4a16_gemv_allgather(const void* A, const void* W_packed, const void* scales, const void* zero_points,
                                    int M, int N, int K, int group_size, int is_signed, const T4BGather* gather,
                                    void* stream) {

@@ -112,6 +112,7 @@ struct DecodeParams {
     int proj_T[kMaxProj];
     int proj_N[kMaxProj];
     uint16_t* proj_C[kMaxProj];
+    int proj_coloff[kMaxProj];  // fused all-gather: first column of each projection in the group buffer
     // fused all-gather (world > 1): each pair of output columns goes, with the
     // call's epoch, as one 64-bit word to every rank's receive buffer
     unsigned long long* recv[8];
@@ -411,6 +412,7 @@ struct MathCtx {
     uint32_t epoch;         // fused all-gather: this call's epoch (0 on one GPU)
     uint16_t* C;            // the CTA's projection: output and its columns
     int N;
+    int col_off;            // fused all-gather: its first column in the group buffer
     bool aborted;
     int group;          // groups done (selects the reduction buffer)
 };
@@ -716,7 +718,7 @@ __device__ __forceinline__ void run_group(const DecodeParams& p, const GroupInfo
             if (col < ncols && (x.lane & 1) == 0) {
                 const unsigned long long word = ((unsigned long long)x.epoch << 32) | (hv | (hi << 16));
                 const size_t o = ((size_t)(x.epoch & 1u) * M + m) * (size_t)(p.n_total >> 1) +
-                                 (size_t)((p.col_offset + col_base + col) >> 1);
+                                 (size_t)((x.col_off + col_base + col) >> 1);
                 for (int g = 0; g < p.world; ++g) st_relaxed_sys_u64(p.recv[g] + o, word);
             }
         }
@@ -874,6 +876,7 @@ gemv_w4_decode_kernel(const __grid_constant__ DecodeMaps<NP> maps, const DecodeP
     x.epoch = 0;
     x.C = p.proj_C[j];
     x.N = p.proj_N[j];
+    x.col_off = p.proj_coloff[j];
     x.aborted = false;
     x.group = 0;
     GroupInfo gi = group_info(p, q, 0);
@@ -1045,11 +1048,14 @@ static bool make_proj_maps(ProjMaps& m, const void* W, const void* S, const void
 // single ops and the fused gather).  Z is NULL (no zero points) or np
 // pointers, all set.  plan_only: run every check and the shared-memory plan,
 // launch nothing (no pointer is read; Z only says whether there are zero
-// points).  ctas, if given, receives each projection's CTA count.
+// points).  ctas, if given, receives each projection's CTA count.  With a
+// fused all-gather, col_offsets gives each projection's first column in the
+// group buffer (NULL: gather->col_offset, one projection).
 static int decode_impl(bool is_signed, const void* A, int np, const void* const* W, const void* const* S,
                        const void* const* Z, void* const* C, const int* N, int M, int K, int group,
-                       const T4BGather* gather, cudaStream_t stream, bool plan_only = false, int* ctas = nullptr) {
-    if (np < 1 || np > kMaxProj || (gather && np != 1)) return T4B_ERR_UNSUPPORTED;
+                       const T4BGather* gather, cudaStream_t stream, bool plan_only = false, int* ctas = nullptr,
+                       const int* col_offsets = nullptr) {
+    if (np < 1 || np > kMaxProj || (gather && np != 1 && !col_offsets)) return T4B_ERR_UNSUPPORTED;
     const bool has_zp = Z != nullptr;
     const int KW = K / 8;
     const int gw = group / 8;
@@ -1114,6 +1120,7 @@ static int decode_impl(bool is_signed, const void* A, int np, const void* const*
         p.proj_T[j] = in ? T[j] : 0;
         p.proj_N[j] = in ? N[j] : 0;
         p.proj_C[j] = (in && C) ? static_cast<uint16_t*>(C[j]) : nullptr;
+        p.proj_coloff[j] = (in && gather) ? (col_offsets ? col_offsets[j] : gather->col_offset) : 0;
     }
     p.T = (int)t_total;
     p.G = used;
@@ -1219,11 +1226,10 @@ int gemv_w4_decode_grouped_plan(int np, const int* N, int M, int K, int group, b
                        nullptr, true, ctas);
 }
 
-int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const void* S, const void* Z, int M, int N,
-                          int K, int group, const T4BGather* g, cudaStream_t stream) {
+// The checks of a T4BGather shared by every projection of a call.
+static int check_gather(const T4BGather* g, int M) {
     if (!g || g->world < 2 || g->world > 8 || g->rank < 0 || g->rank >= g->world) return T4B_ERR_INVALID_VALUE;
-    if (g->col_offset < 0 || g->n_total < 2 || (long long)g->col_offset + N > g->n_total) return T4B_ERR_INVALID_VALUE;
-    if ((g->col_offset | g->n_total | N) & 1) return T4B_ERR_INVALID_VALUE;     // whole column pairs
+    if (g->n_total < 2 || (g->n_total & 1)) return T4B_ERR_INVALID_VALUE;     // whole column pairs
     if ((long long)M * g->n_total >= (1ll << 31)) return T4B_ERR_INVALID_VALUE;
     if (!g->out || !g->counter) return T4B_ERR_NULL_POINTER;
     if (reinterpret_cast<uintptr_t>(g->out) & 3) return T4B_ERR_MISALIGNED;
@@ -1231,7 +1237,31 @@ int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const vo
         if (!g->recv[r]) return T4B_ERR_NULL_POINTER;
         if (reinterpret_cast<uintptr_t>(g->recv[r]) & 7) return T4B_ERR_MISALIGNED;
     }
+    return T4B_OK;
+}
+
+// Columns [off, off + N) of the group buffer: whole column pairs inside it.
+static bool gather_columns_ok(const T4BGather* g, int off, int N) {
+    return off >= 0 && (long long)off + N <= g->n_total && ((off | N) & 1) == 0;
+}
+
+int gemv_w4_decode_gather(bool is_signed, const void* A, const void* W, const void* S, const void* Z, int M, int N,
+                          int K, int group, const T4BGather* g, cudaStream_t stream) {
+    const int st = check_gather(g, M);
+    if (st != T4B_OK) return st;
+    if (!gather_columns_ok(g, g->col_offset, N)) return T4B_ERR_INVALID_VALUE;
     return decode_impl(is_signed, A, 1, &W, &S, Z ? &Z : nullptr, nullptr, &N, M, K, group, g, stream);
+}
+
+int gemv_w4_decode_gather_grouped(bool is_signed, const void* A, int np, const void* const* W, const void* const* S,
+                                  const void* const* Z, const int* N, const int* col_offsets, int M, int K, int group,
+                                  const T4BGather* g, cudaStream_t stream) {
+    const int st = check_gather(g, M);
+    if (st != T4B_OK) return st;
+    if (np < 1 || np > kMaxProj) return T4B_ERR_INVALID_VALUE;
+    for (int j = 0; j < np; ++j)
+        if (!gather_columns_ok(g, col_offsets[j], N[j])) return T4B_ERR_INVALID_VALUE;
+    return decode_impl(is_signed, A, np, W, S, Z, nullptr, N, M, K, group, g, stream, false, nullptr, col_offsets);
 }
 
 }  // namespace t4b

@@ -364,6 +364,7 @@ def _binding():
             addr = lambda f: ctypes.cast(f, ctypes.c_void_p).value    # noqa: E731
             b.init(addr(lib.t4b_fused_w4a16_gemm_u4), addr(lib.t4b_fused_w4a16_gemm_s4),
                    addr(lib.t4b_fused_w4a16_gemv_allgather), addr(lib.t4b_fused_w4a16_gemm_grouped),
+                   addr(lib.t4b_fused_w4a16_gemv_allgather_grouped),
                    addr(lib.t4b_status_string),
                    addr(lib.t4b_last_cuda_error), _lib.T4BError)
         _BIND = b

@@ -208,9 +208,12 @@ class P2PGatherGroup:
     and are overwritten by the group's next call.  Every rank must create its groups
     in the same order and call them in the same order.  Raises RuntimeError
     when the decode kernel does not take a shape (use ShardedGroup, the NCCL
-    path, then)."""
+    path, then).  With ``grouped`` (the default) a group of projections that
+    one grouped launch takes (t4b_fused_w4a16_gemv_allgather_grouped: all s4
+    or all u4, the same K and group size) is called as that one launch
+    instead of one launch per projection."""
 
-    def __init__(self, linears, M, process_group=None):
+    def __init__(self, linears, M, process_group=None, grouped=True):
         self.linears = list(linears)
         self.pg = process_group
         self.world = dist.get_world_size(process_group)
@@ -245,6 +248,15 @@ class P2PGatherGroup:
             everyone = [None] * self.world
             dist.all_gather_object(everyone, self._handle(recv_ptr), group=process_group)
             recv = [recv_ptr if g == self.rank else self._open(everyone[g]) for g in range(self.world)]
+        self._grouped = None
+        if grouped:
+            args = _grouped_args(self.linears)
+            if args is not None:
+                lin0 = self.linears[0]
+                K = lin0.W.size(0) * 8
+                groups = lin0.S.size(0) if lin0.S.dim() == 2 else 1
+                if ops.grouped_plan(self.widths, M, K, K // groups, args[2] is not None) is not None:
+                    self._grouped = args
         self._gathers = []
         for i in range(len(self.linears)):
             g = _lib.T4BGather()
@@ -267,6 +279,12 @@ class P2PGatherGroup:
             rows.append([lin.W.data_ptr(), S.data_ptr(), Z, lin.n_local, K, K // S.size(0),
                          1 if lin.fmt == "s4" else 0, ctypes.addressof(g)])
         self._table = torch.tensor(rows, dtype=torch.int64)
+        if self._grouped is not None:
+            # one launch for the group: the last projection's descriptor
+            # (barrier = 1) with every projection's column offset
+            self._col_offsets = [g.col_offset for g in self._gathers]
+            self._table = torch.tensor([r[:7] + [ctypes.addressof(self._gathers[-1]), off]
+                                        for r, off in zip(rows, self._col_offsets)], dtype=torch.int64)
         self._bind = ops._binding()
 
     def _alloc(self, nbytes):
@@ -289,11 +307,26 @@ class P2PGatherGroup:
 
     def __call__(self, x):
         if self._bind is not None:
-            self._bind.allgather_group(x, self._table, self.M)
+            if self._grouped is not None:
+                self._bind.allgather_grouped(x, self._table, self.M)
+            else:
+                self._bind.allgather_group(x, self._table, self.M)
             return self._views
         if x.size(0) != self.M or x.dtype != torch.float16 or not x.is_contiguous():
             raise RuntimeError(f"the fused gather group takes contiguous fp16 activations of {self.M} rows")
         stream = torch._C._cuda_getCurrentRawStream(self.device.index)
+        if self._grouped is not None:
+            r = self._table.tolist()
+            n = len(r)
+            vp = ctypes.c_void_p * n
+            st = self._lib.t4b_fused_w4a16_gemv_allgather_grouped(
+                x.data_ptr(), n, vp(*[q[0] for q in r]), vp(*[q[1] for q in r]),
+                vp(*[q[2] for q in r]) if r[0][2] else None, (ctypes.c_int * n)(*[q[3] for q in r]),
+                (ctypes.c_int * n)(*[q[8] for q in r]), self.M, r[0][4], r[0][5], r[0][6],
+                ctypes.byref(self._gathers[-1]), stream)
+            if st:
+                _lib.check(st, "t4b_fused_w4a16_gemv_allgather_grouped")
+            return self._views
         fn = self._lib.t4b_fused_w4a16_gemv_allgather
         for lin, g in zip(self.linears, self._gathers):
             K = lin.W.size(0) * 8

@@ -67,6 +67,26 @@ def test_allgather_rejects_bad_descriptors(lib):
                                               ctypes.byref(_gather()), None) == 1   # K not a multiple of 8
 
 
+def test_grouped_allgather_rejects_bad_descriptors(lib):
+    p = ctypes.c_void_p(0x100000)
+    vp2 = ctypes.c_void_p * 2
+    ptrs = vp2(0x100000, 0x200000)
+    i2 = ctypes.c_int * 2
+
+    def call(g, N=(64, 64), offs=(0, 64), n=2, K=4096):
+        return lib.t4b_fused_w4a16_gemv_allgather_grouped(p, n, ptrs, ptrs, None, i2(*N), i2(*offs), 1, K, 128, 1,
+                                                          ctypes.byref(g) if g is not None else None, None)
+    assert call(None) == 2                                   # no descriptor
+    assert call(_gather(), n=0) == 1                         # no projection
+    assert call(_gather(), n=5) == 1                         # more than T4B_GROUPED_MAX
+    assert call(_gather(world=1)) == 1
+    assert call(_gather(rank=3)) == 1
+    assert call(_gather(), offs=(0, 200)) == 1               # second projection past the buffer's row
+    assert call(_gather(), offs=(0, 63)) == 1                # column pairs: offsets even
+    assert call(_gather(fill=False)) == 2                    # buffers missing
+    assert call(_gather(), K=100) == 1                       # K not a multiple of 8
+
+
 def test_group_column_layout():
     offs, total = shard.column_offsets([512, 128, 128], 8)
     assert offs == [0, 4096, 5120] and total == 6144

@@ -2,7 +2,8 @@
 fewer): the ranks (processes; NCCL only to exchange the receive buffers'
 handles) each hold their share of the columns of the projections of two groups -- three projections at M = 1
 and one at M = 3 -- and call them in the order G1, G2, G1, G2, G1 with fresh
-activations each time.  After every call each rank's outputs hold the whole
+activations each time -- G1 as one grouped launch (its three projections in
+one decode launch) and as one launch per projection.  After every call each rank's outputs hold the whole
 projection outputs, equal to the oracle within the GEMV gate, and the device
 error word stays clear."""
 
@@ -42,7 +43,7 @@ def _acts(call, M):
     return np.random.default_rng(100 + call).standard_normal((M, K)).astype(np.float16)
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, grouped):
     import torch.distributed as dist
     from t4_cuda_b200 import ops, shard
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -55,7 +56,9 @@ def _worker(rank, world, port, out_dir):
         for gi, (M, Ns) in enumerate((G1, G2)):
             lins = [shard.ShardedLinear.from_full(torch.from_numpy(W).to(dev), torch.from_numpy(S).to(dev),
                                                   None, "s4") for W, S in _weights(gi, Ns)]
-            groups.append(shard.P2PGatherGroup(lins, M))
+            groups.append(shard.P2PGatherGroup(lins, M, grouped=grouped))
+        # G1 (three s4 projections at M = 1) is one grouped launch when grouped
+        assert (groups[0]._grouped is not None) == grouped
         res = {}
         for c, gi in enumerate(CALLS):
             x = torch.from_numpy(_acts(c, groups[gi].M)).to(dev)
@@ -72,13 +75,14 @@ def _worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("grouped", [True, False])
 @pytest.mark.parametrize("world", [2, 4])
-def test_fused_allgather_ranks(tmp_path, world):
+def test_fused_allgather_ranks(tmp_path, world, grouped):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import oracle
     import torch.multiprocessing as mp
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), grouped), nprocs=world, join=True,
                        start_method="spawn")
     weights = [_weights(0, G1[1]), _weights(1, G2[1])]
     for rank in range(world):

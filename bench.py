@@ -609,10 +609,13 @@ def run_ours(args):
 
     for _ in range(args.warmup):
         run_step()
-    barrier_sync()
     # one event between consecutive steps: the whole region and every step
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    with ClockSampler(local) as clk:
+    # NVML set-up and the sampling thread start before the barrier: their
+    # time differs by rank and would otherwise skew the ranks' starts
+    clk = ClockSampler(local)
+    with clk:
+        barrier_sync()
         evs[0].record()
         for i in range(args.steps):
             run_step()

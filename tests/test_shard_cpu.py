@@ -117,3 +117,28 @@ def test_sharded_group_gloo_world2(tmp_path):
             assert got.shape == ref.shape
             np.testing.assert_allclose(got, ref, rtol=0, atol=0)      # every rank holds the full output
         np.testing.assert_allclose(d["single"], refs[1], rtol=0, atol=0)
+
+
+def test_grouped_args_rules():
+    """Which projection groups ShardedGroup / P2PGatherGroup call as one
+    grouped launch: 2..4 projections, all s4 or all u4, the same K and group
+    size, zero points for all or none."""
+    def lin(K, N, fmt="s4", groups=None, zp=False):
+        G = groups or K // 128
+        W = torch.zeros((K // 8, N), dtype=torch.int32)
+        S = torch.ones((G, N), dtype=torch.float16)
+        Z = torch.zeros((G, N), dtype=torch.float16) if zp else None
+        return shard.ShardedLinear(W, S, Z, fmt)
+    q, k, v = lin(512, 64), lin(512, 16), lin(512, 16)
+    Ws, Ss, Zs, signed = shard._grouped_args([q, k, v])
+    assert [w.size(1) for w in Ws] == [64, 16, 16] and Zs is None and signed is True
+    assert shard._grouped_args([lin(512, 64, "u4"), lin(512, 32, "u4")])[3] is False
+    z = shard._grouped_args([lin(512, 64, zp=True), lin(512, 32, zp=True)])[2]
+    assert z is not None and len(z) == 2
+    assert shard._grouped_args([q]) is None                                   # one projection
+    assert shard._grouped_args([q] * 5) is None                               # more than 4
+    assert shard._grouped_args([q, lin(512, 64, "u4")]) is None               # mixed formats
+    assert shard._grouped_args([q, lin(1024, 64)]) is None                    # different K
+    assert shard._grouped_args([q, lin(512, 64, groups=8)]) is None           # different group size
+    assert shard._grouped_args([q, lin(512, 64, zp=True)]) is None            # zero points for some
+    assert shard._grouped_args([lin(512, 64, "s3"), lin(512, 64, "s3")]) is None   # INT3 is not grouped

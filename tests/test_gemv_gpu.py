@@ -1,6 +1,7 @@
 """Parity of the fused W4A16 GEMV / GEMM with the oracle.
 
-Gate (written here): against the fp32-accumulated
+Gate (the GEMM tolerance of this path's correctness contract, written here):
+against the fp32-accumulated
 product of fp16 activations and contract-dequantized fp16 weights,
     max |y - y_ref| <= 1e-2 * max |y_ref|      (max relative error)
     mean |y - y_ref| <= 1e-3 * mean |y_ref|    (mean absolute error)

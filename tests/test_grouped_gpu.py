@@ -25,6 +25,9 @@ from tests.test_gemv_gpu import assert_gemm_close
 pytestmark = pytest.mark.gpu
 
 LLAMA8B_GROUPS = {"qkv": [4096, 1024, 1024], "gate_up": [14336, 14336]}
+# the Llama-3-70B layer's groups (hidden 8192), whole (one GPU) and as an 8-way column shard sees them
+LLAMA70B_GROUPS = {"qkv": [8192, 1024, 1024], "gate_up": [28672, 28672],
+                   "qkv_shard8": [1024, 128, 128], "gate_up_shard8": [3584, 3584]}
 
 
 def make_group(seed, M, K, Ns, dev, group=128, zp=False):
@@ -63,6 +66,18 @@ def test_llama8b_groups(cuda_device, name, M):
     for j, (C, (W, s, _)) in enumerate(zip(Cs, projs)):
         assert C.shape == (M, Ns[j])
         check(C, (A, W, s, None), rng, True, f"{name}[{j}] M={M} K=4096 N={Ns[j]}")
+
+
+@pytest.mark.parametrize("M", [1, 16])
+@pytest.mark.parametrize("name", sorted(LLAMA70B_GROUPS))
+def test_llama70b_groups(cuda_device, name, M):
+    Ns = LLAMA70B_GROUPS[name]
+    rng, A, projs, At, dev_projs = make_group(8000 + M + sum(Ns) % 97, M, 8192, Ns, cuda_device)
+    Cs = grouped(At, dev_projs)
+    torch.cuda.synchronize(cuda_device)
+    assert ops.device_error(cuda_device) == 0
+    for j, (C, (W, s, _)) in enumerate(zip(Cs, projs)):
+        check(C, (A, W, s, None), rng, True, f"70B {name}[{j}] M={M} K=8192 N={Ns[j]}")
 
 
 @pytest.mark.parametrize("signed", [True, False])

@@ -105,8 +105,8 @@ struct DecodeParams {
     FastDiv kwdiv;      // division by KWp
     // Projections of this launch (one, or a group that shares A): projection
     // j owns CTAs [proj_g0[j], proj_g0[j+1]) and its T = proj_T[j] tiles,
-    // output proj_C[j] of proj_N[j] columns.  T, G, N and C above are those of
-    // a one-projection launch.
+    // output proj_C[j] of proj_N[j] columns.  T and G above are the launch's
+    // totals (the grid is G CTAs), N and C those of projection 0.
     int nproj;
     int proj_g0[kMaxProj + 1];
     int proj_T[kMaxProj];
